@@ -1,0 +1,146 @@
+"""Seeded synthetic workloads for the resolver benchmarks and parity tests.
+
+The reference measures on no public dataset; every input is synthetic.  The
+generators below produce the decode-step top-k traces and table states of the
+five benchmark configurations with numpy's PCG64 generator:
+
+* ``c0``/``c2`` locality: step 0 draws top-k distinct ids by Zipf(s) over
+  positions; every later step keeps ``reuse`` of the previous step's ids
+  (sampled without replacement) and draws the rest by Zipf, re-drawing
+  duplicates.  The Zipf draw uses the LRU simulator's CDF method: rank r has
+  weight 1/r**s and the id is ``searchsorted(cdf, u * total)``
+  (simu/kv_cache_eviction_sim.py:186-195,220-235).
+* ``c1``: per request a 128K-entry table that is -1 except ``resident``
+  uniformly placed entries holding a permutation of slots; queries are
+  distinct, ``hit_frac`` drawn from the resident set.
+* ``c4``: a fixed fraction reused from the previous step and the rest uniform
+  over a 1M-token context.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+NOT_FOUND = -1
+
+
+def zipf_cdf(n: int, s: float) -> np.ndarray:
+    """Cumulative weights of ranks 1..n with weight 1/rank**s (float64)."""
+    return np.cumsum(1.0 / np.arange(1, n + 1, dtype=np.float64) ** s)
+
+
+class LocalityTrace:
+    """Per-request decode-step top-k streams with reuse + Zipf locality."""
+
+    def __init__(self, req_num: int, key_space: int, topk: int = 2048, reuse: float = 0.7,
+                 zipf_s: float = 1.1, seed: int = 0):
+        if topk > key_space:
+            raise ValueError("topk must not exceed key_space")
+        self.req_num = req_num
+        self.key_space = key_space
+        self.topk = topk
+        self.n_reuse = int(round(topk * reuse))
+        self.rng = np.random.Generator(np.random.PCG64(seed))
+        self.cdf = zipf_cdf(key_space, zipf_s)
+        self.total = float(self.cdf[-1])
+        self.prev: np.ndarray | None = None
+
+    def _zipf(self, n: int) -> np.ndarray:
+        u = self.rng.random(n) * self.total
+        return np.minimum(np.searchsorted(self.cdf, u, side="left"), self.key_space - 1)
+
+    def _fill(self, keep: np.ndarray, need: int) -> np.ndarray:
+        """Draw ``need`` Zipf ids not in ``keep`` and distinct, in draw order."""
+        taken = set(keep.tolist())
+        out: list[int] = []
+        batch = max(4 * need, 64)
+        tries = 0
+        while len(out) < need:
+            for v in self._zipf(batch).tolist():
+                if v not in taken:
+                    taken.add(v)
+                    out.append(v)
+                    if len(out) == need:
+                        break
+            tries += 1
+            if tries > 64:  # heavy head: fall back to uniform fill like _fill_unique_tokens
+                while len(out) < need:
+                    v = int(self.rng.integers(0, self.key_space))
+                    if v not in taken:
+                        taken.add(v)
+                        out.append(v)
+        return np.asarray(out, np.int32)
+
+    def step(self) -> np.ndarray:
+        """Next step's [req_num, topk] int32 ids (distinct within a row)."""
+        rows = np.empty((self.req_num, self.topk), np.int32)
+        for r in range(self.req_num):
+            if self.prev is None:
+                keep = np.zeros(0, np.int32)
+            else:
+                keep = self.rng.permutation(self.prev[r])[: self.n_reuse]
+            fresh = self._fill(keep, self.topk - keep.size)
+            row = np.concatenate([keep, fresh])
+            rows[r] = self.rng.permutation(row)
+        self.prev = rows
+        return rows
+
+
+def lookup_only_case(req_num: int = 64, index_size: int = 128 * 1024, resident: int = 4096,
+                     query_len: int = 2048, hit_frac: float = 0.85, seed: int = 1):
+    """Table + queries of the lookup-only workload (64 x 128K table, 64 x 2048 queries)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    table = np.full((req_num, index_size), NOT_FOUND, np.int32)
+    query = np.empty((req_num, query_len), np.int32)
+    n_hit = int(round(query_len * hit_frac))
+    for r in range(req_num):
+        pos = rng.choice(index_size, size=resident, replace=False).astype(np.int32)
+        table[r, pos] = rng.permutation(resident).astype(np.int32)
+        hits = rng.choice(pos, size=n_hit, replace=False)
+        mask = np.ones(index_size, bool)
+        mask[pos] = False
+        absent = np.flatnonzero(mask)
+        misses = rng.choice(absent, size=query_len - n_hit, replace=False)
+        query[r] = rng.permutation(np.concatenate([hits, misses]).astype(np.int32))
+    return table, query
+
+
+class UniformReuseTrace:
+    """Stress trace: ``reuse`` of the previous ids kept, the rest uniform over the context."""
+
+    def __init__(self, req_num: int, key_space: int, topk: int = 2048, reuse: float = 0.2, seed: int = 4):
+        self.req_num, self.key_space, self.topk = req_num, key_space, topk
+        self.n_reuse = int(round(topk * reuse))
+        self.rng = np.random.Generator(np.random.PCG64(seed))
+        self.prev: np.ndarray | None = None
+
+    def step(self) -> np.ndarray:
+        rows = np.empty((self.req_num, self.topk), np.int32)
+        for r in range(self.req_num):
+            keep = np.zeros(0, np.int32) if self.prev is None else self.rng.permutation(self.prev[r])[: self.n_reuse]
+            taken = set(keep.tolist())
+            fresh: list[int] = []
+            while len(fresh) < self.topk - keep.size:
+                for v in self.rng.integers(0, self.key_space, 2 * self.topk).tolist():
+                    if v not in taken:
+                        taken.add(v)
+                        fresh.append(v)
+                        if len(fresh) == self.topk - keep.size:
+                            break
+            rows[r] = self.rng.permutation(np.concatenate([keep, np.asarray(fresh, np.int32)]))
+        self.prev = rows
+        return rows
+
+
+def record_addresses(req_num: int, key_space: int, pool_rows: int, salt: int = 0x9E3779B1) -> np.ndarray:
+    """[req_num, key_space] int32 row index of each (request, key) record in the host pool.
+
+    A multiplicative hash scatters records over a pool of ``pool_rows`` rows so
+    that a bounded pinned pool can stand in for a full per-token backing store
+    (several keys may share a row; every check uses the same table).
+    """
+    r = np.arange(req_num, dtype=np.uint64)[:, None]
+    k = np.arange(key_space, dtype=np.uint64)[None, :]
+    h = (r * np.uint64(key_space) + k) * np.uint64(salt) + np.uint64(0x7F4A7C15)
+    h ^= h >> np.uint64(29)
+    return (h % np.uint64(pool_rows)).astype(np.int32)
