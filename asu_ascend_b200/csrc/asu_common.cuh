@@ -1,0 +1,80 @@
+// Shared device helpers for the ASU resolver kernels (sm_100a).
+//
+// Conventions used by every kernel in this library:
+//  * One request row per CTA for the stateful ops: every read-modify-write of a
+//    request's maps happens inside one CTA, ordered by __syncthreads().  Mutable
+//    state is read with ld.global.cg (L2, never a stale L1 line) and written
+//    with st.global.cg.
+//  * Kernels never trap.  Problems are OR-ed into a per-request int32 status
+//    word (ASU_ST_* bits) when the caller passes one, and the offending
+//    element is skipped.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/asu_b200.h"
+
+namespace asu {
+
+constexpr int32_t kNotFound = -1;
+constexpr int32_t kClaimBase = INT32_MIN;  // claim value of query position p: kClaimBase + p
+
+__host__ __device__ __forceinline__ uint32_t hash32(uint32_t x) {
+    // Integer mixer of ops/asu_hbm_index_maintain_aicpu_kernel.aicpu:25-33 (same constants, same steps).
+    x ^= x >> 16;
+    x *= 0x7feb352dU;
+    x ^= x >> 15;
+    x *= 0x846ca68bU;
+    x ^= x >> 16;
+    return x;
+}
+
+__device__ __forceinline__ int32_t ld_cg(const int32_t* p) { return __ldcg(p); }
+__device__ __forceinline__ void st_cg(int32_t* p, int32_t v) { __stcg(p, v); }
+
+__device__ __forceinline__ void flag_status(int32_t* status, int row, int32_t bits) {
+    if (status != nullptr) atomicOr(status + row, bits);
+}
+
+// Block-wide exclusive scan of one int per thread (blockDim.x a multiple of 32, <= 1024).
+// `warp_sums` must hold 33 ints of shared memory.  Returns the exclusive prefix and
+// writes the block total to *total.  Contains three __syncthreads() (the last one lets
+// back-to-back scans reuse `warp_sums`); every thread of the block must call it.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int nwarps = blockDim.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, d);
+        if (lane >= d) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < nwarps ? warp_sums[lane] : 0;
+        int s = w;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, s, d);
+            if (lane >= d) s += y;
+        }
+        if (lane < nwarps) warp_sums[lane] = s - w;  // exclusive warp offsets
+        if (lane == 31) warp_sums[32] = s;
+    }
+    __syncthreads();
+    int res = warp_sums[warp] + x - v;
+    *total = warp_sums[32];
+    __syncthreads();
+    return res;
+}
+
+}  // namespace asu
+
+// Host-side launch-error helper shared by the entry points.
+static inline int asu_launch_status() {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? ASU_OK : ASU_ERR_CUDA_BASE + static_cast<int>(e);
+}

@@ -1,0 +1,144 @@
+// Swap-in gather: copy the KV rows of newly installed keys from a pinned, GPU-mapped host
+// row pool into the HBM slot pool.
+//
+// Reference behaviour: the v0/v0.1 designs fetch each missed (request, layer, token) record
+// from MicroKV over a Unix socket, deserialize it on the CPU and copy it to the device
+// (docs/v0.1/kv-cache-offload-v0.1-real-ops-design.md:293-312; MicroKV/src/server.cpp:220-251).
+// The bytes that land in slot `s` are the record's bytes, unchanged.
+//
+// B200 design: zero-copy.  The host pool is page-locked and mapped, so the GPU reads it
+// directly over the host link with 16-byte loads and writes 16-byte stores into HBM; no
+// host thread, no staging copy, no synchronisation with the CPU.  Work unit: one warp per
+// 32 query positions of one request.  The warp ballots the install flags, compacts the
+// (source row, destination row) pairs of its installs into shared memory, and then copies
+// the flattened (row, 16-byte chunk) space lane-strided with 8 loads in flight per lane
+// before their stores, so a 656-byte DSA row (41 chunks) and a 41,984-byte block row both
+// keep the link busy.  Grid: enough warps for every group, capped at 8 CTAs per SM.
+#include "asu_common.cuh"
+
+namespace asu {
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kUnroll = 8;
+
+__global__ void __launch_bounds__(kWarps * 32)
+swapin_kernel(const int4* host, int64_t pool_rows, uint32_t cpr, const int32_t* __restrict__ rec, uint32_t K,
+              const int32_t* __restrict__ query, const int32_t* __restrict__ slot,
+              const uint8_t* __restrict__ inst, uint32_t Q, int4* __restrict__ pool, uint32_t S, uint32_t R,
+              int32_t* status) {
+    __shared__ int64_t src_row[kWarps][32];
+    __shared__ int64_t dst_row[kWarps][32];
+    const int lane = threadIdx.x & 31;
+    const int w = threadIdx.x >> 5;
+    const uint32_t groups_per_row = (Q + 31) / 32;
+    const uint64_t total_groups = static_cast<uint64_t>(R) * groups_per_row;
+    for (uint64_t g = static_cast<uint64_t>(blockIdx.x) * kWarps + w; g < total_groups;
+         g += static_cast<uint64_t>(gridDim.x) * kWarps) {
+        const uint32_t r = static_cast<uint32_t>(g / groups_per_row);
+        const uint32_t pos = static_cast<uint32_t>(g - static_cast<uint64_t>(r) * groups_per_row) * 32 + lane;
+        const uint64_t qi = static_cast<uint64_t>(r) * Q + pos;
+        const bool flag = pos < Q && __ldg(inst + qi) != 0;
+        if (__ballot_sync(0xffffffffu, flag) == 0u) continue;
+        bool ok = false;
+        int64_t src = 0, dst = 0;
+        if (flag) {
+            const int32_t key = __ldg(query + qi);
+            const int32_t s = __ldg(slot + qi);
+            int32_t bits = 0;
+            if (static_cast<uint32_t>(key) >= K) {
+                bits |= ASU_ST_BAD_QUERY;
+            } else if (static_cast<uint32_t>(s) >= S) {
+                bits |= ASU_ST_BAD_STATE;
+            } else {
+                const int32_t row = __ldg(rec + static_cast<uint64_t>(r) * K + key);
+                if (row < 0 || row >= pool_rows) {
+                    bits |= ASU_ST_BAD_SOURCE;
+                } else {
+                    ok = true;
+                    src = row;
+                    dst = static_cast<int64_t>(r) * S + s;
+                }
+            }
+            if (bits) flag_status(status, r, bits);
+        }
+        const unsigned okmask = __ballot_sync(0xffffffffu, ok);
+        if (ok) {
+            const int rank = __popc(okmask & ((1u << lane) - 1u));
+            src_row[w][rank] = src;
+            dst_row[w][rank] = dst;
+        }
+        __syncwarp();
+        const uint32_t n = __popc(okmask);
+        const uint32_t total = n * cpr;
+        for (uint32_t base = 0; base < total; base += 32 * kUnroll) {
+            int4 buf[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const uint32_t c = base + u * 32 + lane;
+                if (c < total) {
+                    const uint32_t ri = c / cpr;
+                    const uint32_t ch = c - ri * cpr;
+                    buf[u] = host[src_row[w][ri] * cpr + ch];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const uint32_t c = base + u * 32 + lane;
+                if (c < total) {
+                    const uint32_t ri = c / cpr;
+                    const uint32_t ch = c - ri * cpr;
+                    pool[dst_row[w][ri] * cpr + ch] = buf[u];
+                }
+            }
+        }
+        __syncwarp();
+    }
+}
+
+}  // namespace
+}  // namespace asu
+
+using namespace asu;
+
+extern "C" int asu_swapin_gather(void* stream, const void* host_pool, int64_t pool_rows, uint32_t row_bytes,
+                                 const int32_t* record_addr, uint32_t key_space, const int32_t* query,
+                                 const int32_t* slot, const uint8_t* install_mask, uint32_t query_count,
+                                 void* slot_pool, uint32_t slot_count, uint32_t req_num, int32_t* status) {
+    if (req_num == 0 || query_count == 0) return ASU_OK;
+    if (!host_pool || !record_addr || !query || !slot || !install_mask || !slot_pool || pool_rows <= 0 ||
+        row_bytes == 0 || key_space == 0 || slot_count == 0)
+        return ASU_ERR_ARG;
+    if (row_bytes % 16 != 0 || reinterpret_cast<uintptr_t>(host_pool) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(slot_pool) % 16 != 0)
+        return ASU_ERR_ALIGN;
+    const uint64_t groups = static_cast<uint64_t>(req_num) * ((query_count + 31) / 32);
+    uint64_t grid = (groups + kWarps - 1) / kWarps;
+    if (grid > 148ull * 8ull) grid = 148ull * 8ull;
+    swapin_kernel<<<static_cast<uint32_t>(grid), kWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const int4*>(host_pool), pool_rows, row_bytes / 16, record_addr, key_space, query, slot,
+        install_mask, query_count, static_cast<int4*>(slot_pool), slot_count, req_num, status);
+    return asu_launch_status();
+}
+
+extern "C" int asu_host_pool_alloc(uint64_t bytes, void** host_ptr, void** device_ptr) {
+    if (!host_ptr || bytes == 0) return ASU_ERR_ARG;
+    void* h = nullptr;
+    cudaError_t e = cudaHostAlloc(&h, bytes, cudaHostAllocPortable | cudaHostAllocMapped);
+    if (e != cudaSuccess) return ASU_ERR_CUDA_BASE + static_cast<int>(e);
+    void* d = nullptr;
+    e = cudaHostGetDevicePointer(&d, h, 0);
+    if (e != cudaSuccess) {
+        cudaFreeHost(h);
+        return ASU_ERR_CUDA_BASE + static_cast<int>(e);
+    }
+    *host_ptr = h;
+    if (device_ptr) *device_ptr = d;
+    return ASU_OK;
+}
+
+extern "C" int asu_host_pool_free(void* host_ptr) {
+    if (!host_ptr) return ASU_OK;
+    cudaError_t e = cudaFreeHost(host_ptr);
+    return e == cudaSuccess ? ASU_OK : ASU_ERR_CUDA_BASE + static_cast<int>(e);
+}

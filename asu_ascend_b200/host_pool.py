@@ -1,0 +1,83 @@
+"""Pinned, GPU-mapped host row pool and the swap-in gather into the HBM slot pool.
+
+The pool replaces the MicroKV backing store of the reference's v0/v0.1 designs
+(MicroKV/src/kv_store.h:14-37 keyed by (request, layer, token, type);
+MicroKV/python/microkv/client.py:43-63): records are fixed-size rows in page-locked,
+mapped host memory, and ``record_addr[r, key]`` gives the row of request r's key (a
+dense index instead of a hash map).  ``swapin`` copies the rows of every installing
+position into ``slot_pool[r, slot]`` with one kernel that reads host memory directly.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from ._lib import check, lib, raise_on_status
+
+
+class HostRowPool:
+    def __init__(self, rows: int, row_bytes: int):
+        if rows <= 0 or row_bytes <= 0 or row_bytes % 16:
+            raise ValueError("rows must be positive and row_bytes a positive multiple of 16")
+        self.rows, self.row_bytes = rows, row_bytes
+        self.nbytes = rows * row_bytes
+        host = ctypes.c_void_p()
+        dev = ctypes.c_void_p()
+        check(lib.asu_host_pool_alloc(self.nbytes, ctypes.byref(host), ctypes.byref(dev)), "asu_host_pool_alloc")
+        self._host = host.value
+        self.device_ptr = dev.value
+        buf = (ctypes.c_uint8 * self.nbytes).from_address(self._host)
+        self.array = np.frombuffer(buf, dtype=np.uint8).reshape(rows, row_bytes)
+        self.tensor = torch.from_numpy(self.array)  # CPU view of the same pinned bytes
+
+    def fill_random(self, seed: int) -> None:
+        rng = np.random.Generator(np.random.PCG64(seed))
+        step = max(1, (64 << 20) // self.row_bytes)
+        for i in range(0, self.rows, step):
+            j = min(self.rows, i + step)
+            self.array[i:j] = rng.integers(0, 256, (j - i, self.row_bytes), dtype=np.uint8)
+
+    def close(self) -> None:
+        if getattr(self, "_host", None):
+            self.array = None
+            self.tensor = None
+            check(lib.asu_host_pool_free(self._host), "asu_host_pool_free")
+            self._host = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def swapin(self, record_addr: torch.Tensor, query: torch.Tensor, slot: torch.Tensor, install: torch.Tensor,
+               slot_pool: torch.Tensor, status: torch.Tensor | None = None,
+               stream: torch.cuda.Stream | None = None) -> None:
+        """slot_pool[r, slot[r,p]] = pool[record_addr[r, query[r,p]]] for every p with install[r,p]."""
+        dev = slot_pool.device
+        R, Q = query.shape
+        for name, t in (("record_addr", record_addr), ("query", query), ("slot", slot)):
+            if t.dtype != torch.int32 or t.device != dev or not t.is_contiguous():
+                raise RuntimeError(f"{name} must be a contiguous int32 CUDA tensor on {dev}")
+        if install.dtype not in (torch.bool, torch.uint8) or install.shape != query.shape:
+            raise RuntimeError("install must be a bool/uint8 tensor shaped like query")
+        if slot_pool.dim() < 2 or not slot_pool.is_contiguous() or slot_pool.shape[0] != R:
+            raise RuntimeError("slot_pool must be a contiguous [R, slots, row] tensor")
+        row = slot_pool[0, 0].numel() * slot_pool.element_size()
+        if row != self.row_bytes:
+            raise RuntimeError(f"slot_pool rows are {row} bytes, the host pool's are {self.row_bytes}")
+        if record_addr.dim() != 2 or record_addr.shape[0] != R:
+            raise RuntimeError("record_addr must be [R, key_space]")
+        s = (stream or torch.cuda.current_stream(dev)).cuda_stream
+        with torch.cuda.device(dev):
+            check(lib.asu_swapin_gather(
+                s, self.device_ptr, self.rows, self.row_bytes, record_addr.data_ptr(), record_addr.shape[1],
+                query.data_ptr(), slot.data_ptr(), install.data_ptr(), Q, slot_pool.data_ptr(), slot_pool.shape[1],
+                R, None if status is None else status.data_ptr()), "asu_swapin_gather")
+
+
+def check_status(status: torch.Tensor, what: str, ignore: int = 0) -> None:
+    raise_on_status(status, what, ignore)
