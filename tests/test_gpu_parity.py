@@ -1,0 +1,568 @@
+"""GPU parity: every CUDA kernel, called through the C ABI (directly or via the torch ops),
+against the oracle and the reference-generated golden vectors.  Bit-exact everywhere
+(integer / index / byte work)."""
+
+import ctypes
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import asu_oracle as O
+from tests import cases as C
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    import asu_ascend_b200
+
+    asu_ascend_b200.load()
+    from asu_ascend_b200 import ops
+
+    ops.set_status_checks(True)
+    yield
+    ops.set_status_checks(False)
+
+
+def T(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def N(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def digest(*arrays):
+    h = hashlib.sha256()
+    for a in arrays:
+        a = np.ascontiguousarray(a)
+        h.update(str(a.dtype).encode())
+        h.update(str(a.shape).encode())
+        h.update(a.tobytes())
+    return h.hexdigest()
+
+
+def stream_ptr():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+# ------------------------------------------------------------------ gather / update
+
+@pytest.mark.parametrize("name,builder", [("single", C.gather_single_case), ("multi", C.gather_multi_case),
+                                          ("dup", C.gather_dup_case)])
+def test_gather_update_matches_golden(golden, name, builder):
+    from asu_ascend_b200 import hbm_lookup_update as H
+
+    g = golden("gather")
+    states, q, new, seed, pct = builder()
+    single = name == "single"
+    st = T(states[0] if single else states)
+    qq = T(q[0] if single else q)
+    nn = T(new[0] if single else new)
+    keys = torch.zeros_like(st)
+    out = H.lookup_random_update(keys, st, qq, nn, seed=seed, update_percent=pct)
+    np.testing.assert_array_equal(N(out).reshape(g[f"{name}_out"].shape), g[f"{name}_out"])
+    exp_states = C.apply_changes(states, g[f"{name}_upd_idx"], g[f"{name}_upd_val"])
+    np.testing.assert_array_equal(N(st).reshape(exp_states.shape), exp_states)
+    # lookup_only on a fresh copy, update_only on another
+    st2 = T(states[0] if single else states)
+    out2 = H.lookup_only(keys, st2, qq)
+    np.testing.assert_array_equal(N(out2).reshape(g[f"{name}_out"].shape), g[f"{name}_out"])
+    H.update_only(keys, st2, qq, nn, seed=seed, update_percent=pct)
+    np.testing.assert_array_equal(N(st2).reshape(exp_states.shape), exp_states)
+
+
+def test_gather_padded_layout_of_the_c_launcher():
+    """hbm_lookup_vec_do writes [req, align64(query_len)] rows with zero padding (kernel.cpp:104-131)."""
+    from asu_ascend_b200._lib import lib
+
+    states, q, _, _, _ = C.gather_multi_case()   # query_len 513 -> padded 576
+    st, qq = T(states), T(q)
+    out = torch.full((4, 576), 12345, dtype=torch.int32, device=DEV)
+    assert lib.hbm_lookup_vec_do(8, stream_ptr(), None, st.data_ptr(), qq.data_ptr(), out.data_ptr(), 4, 513, -1) == 0
+    o = N(out)
+    exp, _ = O.gather_lookup(states, q)
+    np.testing.assert_array_equal(o[:, :513], exp)
+    assert (o[:, 513:] == 0).all()
+
+
+def test_lookup_only_workload_full_size():
+    """Lookup-only workload: 64 x 128K table (4096 resident), 64 x 2048 distinct queries, ~85% hits."""
+    from asu_ascend_b200 import hbm_lookup_update as H
+    from asu_ascend_b200.workloads import lookup_only_case
+
+    table, query = lookup_only_case()
+    out, hit = H.lookup(T(table), T(query))
+    exp, exp_hit = O.gather_lookup(table, query)
+    np.testing.assert_array_equal(N(out), exp)
+    np.testing.assert_array_equal(N(hit), exp_hit)
+    assert 0.8 < exp_hit.mean() < 0.9
+
+
+def test_gather_out_of_range_keys_flag_status():
+    from asu_ascend_b200 import hbm_lookup_update as H
+
+    table = np.arange(64, dtype=np.int32).reshape(2, 32)
+    q = np.array([[0, 31, 32, -1], [5, 99, 3, 2]], np.int32)
+    status = torch.zeros(2, dtype=torch.int32, device=DEV)
+    out, hit = H.lookup(T(table), T(q), status=status)
+    assert N(out).tolist() == [[0, 31, -1, -1], [37, -1, 35, 34]]
+    assert N(status).tolist() == [1, 1]
+
+
+# ------------------------------------------------------------------ ops contract
+
+@pytest.mark.parametrize("pattern", ["hit", "miss", "mixed"])
+def test_ops_lookup_matches_golden(golden, pattern):
+    g = golden("ops")
+    index, s2i, fs, fh, q = C.make_index_case(2, pattern)
+    ti, ts, tf, th, tq = T(index), T(s2i), T(fs), T(fh), T(q)
+    slot_out = torch.ops._C_ascend.asu_hbm_index_lookup(ti, ts, tf, th, tq, 2)
+    np.testing.assert_array_equal(N(slot_out), g[f"lookup_{pattern}_slot_out"])
+    np.testing.assert_array_equal(N(th), g[f"lookup_{pattern}_free_head"])
+    np.testing.assert_array_equal(N(ti), C.apply_changes(index, g[f"lookup_{pattern}_index_idx"],
+                                                         g[f"lookup_{pattern}_index_val"]))
+    np.testing.assert_array_equal(N(ts), C.apply_changes(s2i, g[f"lookup_{pattern}_s2i_idx"],
+                                                         g[f"lookup_{pattern}_s2i_val"]))
+
+
+def test_ops_lookup_through_reference_c_launcher(golden):
+    """The ctypes call shape of ops/scripts/asu_hbm_index_common.py:319-331."""
+    from asu_ascend_b200._lib import lib
+
+    g = golden("ops")
+    index, s2i, fs, fh, q = C.make_index_case(2, "mixed")
+    ti, ts, tf, th, tq = T(index), T(s2i), T(fs), T(fh), T(q)
+    so = torch.empty((2, C.QUERY_COUNT), dtype=torch.int32, device=DEV)
+    rc = lib.asu_hbm_index_lookup_do(2, stream_ptr(), ti.data_ptr(), ts.data_ptr(), tf.data_ptr(), th.data_ptr(),
+                                     tq.data_ptr(), so.data_ptr(), 2)
+    assert rc == 0
+    np.testing.assert_array_equal(N(so), g["lookup_mixed_slot_out"])
+    np.testing.assert_array_equal(N(th), g["lookup_mixed_free_head"])
+
+
+@pytest.mark.parametrize("ratio", [0.25, 1.0, 0.5])
+def test_ops_maintain_matches_golden(golden, ratio):
+    g = golden("ops")
+    tag = f"maintain_{int(ratio * 100)}"
+    index, s2i, fs, fh, lq = C.make_maintain_case(3, ratio)
+    ti, ts, tf, th, tl = T(index), T(s2i), T(fs), T(fh), T(lq)
+    torch.ops._C_ascend.asu_hbm_index_maintain(ti, ts, tf, th, tl, 3, int(g[f"{tag}_seed"][0]))
+    np.testing.assert_array_equal(N(tf), g[f"{tag}_free_slots"])
+    np.testing.assert_array_equal(N(th), g[f"{tag}_free_head"])
+    np.testing.assert_array_equal(N(ti), C.apply_changes(index, g[f"{tag}_index_idx"], g[f"{tag}_index_val"]))
+    np.testing.assert_array_equal(N(ts), C.apply_changes(s2i, g[f"{tag}_s2i_idx"], g[f"{tag}_s2i_val"]))
+
+
+def test_ops_maintain_through_reference_c_launcher(golden):
+    from asu_ascend_b200._lib import lib
+
+    g = golden("ops")
+    index, s2i, fs, fh, lq = C.make_maintain_case(3, 0.25)
+    ti, ts, tf, th, tl = T(index), T(s2i), T(fs), T(fh), T(lq)
+    rc = lib.asu_hbm_index_maintain_do(1, stream_ptr(), ti.data_ptr(), ts.data_ptr(), tf.data_ptr(), th.data_ptr(),
+                                       tl.data_ptr(), 3, int(g["maintain_25_seed"][0]))
+    assert rc == 0
+    np.testing.assert_array_equal(N(tf), g["maintain_25_free_slots"])
+    np.testing.assert_array_equal(N(th), g["maintain_25_free_head"])
+
+
+def test_ops_chained_rounds_match_golden(golden):
+    g = golden("ops")
+    index, s2i, fs, fh, _ = C.make_index_case(2, "hit")
+    ti, ts, tf, th = T(index), T(s2i), T(fs), T(fh)
+    for k in range(3):
+        so = torch.ops.asu.asu_hbm_index_lookup(ti, ts, tf, th, T(g[f"chain{k}_query"]), 2)
+        np.testing.assert_array_equal(N(so), g[f"chain{k}_slot_out"])
+        np.testing.assert_array_equal(N(th), g[f"chain{k}_head_after_lookup"])
+        torch.ops.asu.asu_hbm_index_maintain(ti, ts, tf, th, so, 2, int(g[f"chain{k}_seed"][0]))
+        np.testing.assert_array_equal(N(th), g[f"chain{k}_head_after_maintain"])
+        np.testing.assert_array_equal(N(tf), g[f"chain{k}_free_slots"])
+    assert digest(N(ti), N(ts)) == str(g["chain_final_digest"][0])
+
+
+def test_ops_random_small_sizes_against_oracle():
+    """Sized entry points on random small states with duplicates: 4 chained lookup -> maintain rounds."""
+    rng = np.random.Generator(np.random.PCG64(3))
+    R, IS, S, Q = 5, 300, 64, 40
+    index = np.full((R, IS), -1, np.int32)
+    s2i = np.full((R, S), -1, np.int32)
+    for r in range(R):  # 48 residents in slots 0..47, free list 48..63
+        keys = rng.choice(IS, 48, replace=False).astype(np.int32)
+        index[r, keys] = np.arange(48, dtype=np.int32)
+        s2i[r, :48] = keys
+    fs = np.tile(np.arange(48, S, dtype=np.int32), (R, 1))
+    fh = np.zeros(R, np.int32)
+    ti, ts, tf, th = T(index), T(s2i), T(fs), T(fh)
+    for rnd in range(4):
+        q = np.empty((R, Q), np.int32)
+        for r in range(R):
+            resident = np.flatnonzero(index[r] >= 0)
+            absent = np.setdiff1d(np.arange(IS), resident)
+            miss = rng.choice(absent, 10, replace=False)
+            row = rng.choice(np.concatenate([resident, miss]), Q)  # duplicates on purpose
+            row[:10] = miss
+            q[r] = rng.permutation(row)
+        so_e, index, s2i, fh = O.ops_lookup_allocate(index, s2i, fs, fh, q)
+        so = torch.ops.asu.asu_hbm_index_lookup(ti, ts, tf, th, T(q), R)
+        np.testing.assert_array_equal(N(so), so_e)
+        np.testing.assert_array_equal(N(ti), index)
+        np.testing.assert_array_equal(N(ts), s2i)
+        np.testing.assert_array_equal(N(th), fh)
+        seed = int(rng.integers(0, 2**32))
+        lq = so_e[:, : Q // 2].copy()  # protects <= 20 of >= 58 occupied slots: the ring always terminates
+        index, s2i, fs, fh = O.ops_maintain(index, s2i, fs, fh, lq, seed)
+        torch.ops.asu.asu_hbm_index_maintain(ti, ts, tf, th, T(lq), R, seed)
+        np.testing.assert_array_equal(N(ti), index)
+        np.testing.assert_array_equal(N(ts), s2i)
+        np.testing.assert_array_equal(N(tf), fs)
+        np.testing.assert_array_equal(N(th), fh)
+
+
+def test_ops_error_status_instead_of_undefined_behaviour():
+    from asu_ascend_b200._lib import AsuError
+
+    index = np.full((1, 16), -1, np.int32)
+    s2i = np.full((1, 8), -1, np.int32)
+    fs = np.array([[4, 5]], np.int32)
+    # free list overrun: 3 misses, 2 free entries
+    with pytest.raises(AsuError, match="FREE_EXHAUSTED"):
+        torch.ops.asu.asu_hbm_index_lookup(T(index), T(s2i), T(fs), T(np.zeros(1, np.int32)),
+                                           T(np.array([[1, 2, 3]], np.int32)), 1)
+    # maintain with nothing evictable: the reference would spin forever
+    with pytest.raises(AsuError, match="RING_EXHAUSTED"):
+        torch.ops.asu.asu_hbm_index_maintain(T(index), T(s2i), T(np.zeros((1, 2), np.int32)),
+                                             T(np.array([1], np.int32)), T(np.zeros((1, 2), np.int32)), 1, 0)
+    # out-of-range query id
+    with pytest.raises(AsuError, match="BAD_QUERY"):
+        torch.ops.asu.asu_hbm_index_lookup(T(index), T(s2i), T(np.array([[4, 5, 6]], np.int32)),
+                                           T(np.zeros(1, np.int32)), T(np.array([[16]], np.int32)), 1)
+
+
+# ------------------------------------------------------------------ batch LRU
+
+def _simt_state(slot_tokens, cap=32):
+    t2s = np.full((1, cap), -1, np.int32)
+    for s, t in enumerate(slot_tokens):
+        if t >= 0:
+            t2s[0, t] = s
+    return t2s, np.asarray([slot_tokens], np.int32), np.arange(len(slot_tokens), dtype=np.int16)[None, :]
+
+
+@pytest.mark.parametrize("slots,query,exp_slots,exp_mask,exp_lru,exp_s2t", [
+    ([0, 1, 2, 3], [2, 0], [2, 0], [False, False], [1, 3, 0, 2], [0, 1, 2, 3]),
+    ([1, 4, 2, 5], [4, 6, 7], [1, 0, 2], [False, True, True], [3, 0, 2, 1], [6, 4, 7, 5]),
+    ([0, 1, 2, 3], [4, 4, -1, 1], [0, 0, -1, 1], [True, False, False, False], [2, 3, 0, 1], [4, 1, 2, 3]),
+    ([-1, -1, 2, 3], [4, 3], [0, 3], [True, False], [1, 2, 0, 3], [4, -1, 2, 3]),
+])
+def test_batch_lru_reference_unit_vectors(slots, query, exp_slots, exp_mask, exp_lru, exp_s2t):
+    """pta-ops/asu_hbm_index_lookup_simt/tests/test_reference.py:37-80 on the GPU kernel."""
+    t2s, s2t, lru = _simt_state(slots)
+    tt, ts, tl = T(t2s), T(s2t), T(lru)
+    sid, mask = torch.ops._C_ascend.asu_hbm_index_lookup_simt(tt, ts, tl, T(np.asarray([query], np.int32)), 1)
+    assert N(sid)[0].tolist() == exp_slots
+    assert N(mask)[0].tolist() == exp_mask
+    assert N(tl)[0].tolist() == exp_lru
+    assert N(ts)[0].tolist() == exp_s2t
+
+
+def test_batch_lru_matches_golden_full_size(golden):
+    g = golden("batch_lru")
+    R = 2
+    t2s, s2t, lru = C.simt_full_resident_state()
+    tt, ts, tl = T(np.stack([t2s] * R)), T(np.stack([s2t] * R)), T(np.stack([lru] * R))
+    for rnd in range(3):
+        q = np.stack([g[f"r{r}_q{rnd}"] for r in range(R)])
+        sid, mask = torch.ops.asu.asu_hbm_index_lookup_simt(tt, ts, tl, T(q), R)
+        for r in range(R):
+            np.testing.assert_array_equal(N(sid)[r], g[f"r{r}_slot{rnd}"])
+            np.testing.assert_array_equal(N(mask)[r], g[f"r{r}_mask{rnd}"])
+            np.testing.assert_array_equal(N(tl)[r], g[f"r{r}_lru{rnd}"])
+            np.testing.assert_array_equal(N(ts)[r], g[f"r{r}_s2t{rnd}"])
+            assert digest(N(tt)[r]) == str(g[f"r{r}_t2s_digest{rnd}"][0])
+
+
+def test_batch_lru_through_reference_c_launcher():
+    from asu_ascend_b200._lib import lib
+
+    t2s, s2t, lru = (np.stack([a]) for a in C.simt_full_resident_state())
+    q = (np.arange(C.QUERY_COUNT, dtype=np.int32)[None, :] * 3) % (C.SLOT_COUNT * 2)
+    tt, ts, tl, tq = T(t2s), T(s2t), T(lru), T(q)
+    sid = torch.empty((1, C.QUERY_COUNT), dtype=torch.int32, device=DEV)
+    mask = torch.empty((1, C.QUERY_COUNT), dtype=torch.bool, device=DEV)
+    ws = torch.empty(31492, dtype=torch.int32, device=DEV)
+    assert lib.asu_hbm_index_lookup_simt_do(stream_ptr(), tt.data_ptr(), ts.data_ptr(), tl.data_ptr(), tq.data_ptr(),
+                                            sid.data_ptr(), mask.data_ptr(), ws.data_ptr(), 1) == 0
+    e_t2s, e_s2t, e_lru = t2s[0].tolist(), s2t[0].tolist(), lru[0].astype(np.int32).tolist()
+    es, em = O.batch_lru(q[0].tolist(), e_t2s, e_s2t, e_lru)
+    np.testing.assert_array_equal(N(sid)[0], es)
+    np.testing.assert_array_equal(N(mask)[0], em)
+    np.testing.assert_array_equal(N(tl)[0], e_lru)
+
+
+def test_batch_lru_no_victim_leaves_state_unchanged():
+    from asu_ascend_b200._lib import AsuError
+
+    t2s, s2t, lru = _simt_state([0, 1, 2, 3])
+    tt, ts, tl = T(t2s), T(s2t), T(lru)
+    with pytest.raises(AsuError, match="NO_VICTIM"):  # 2 hits + 3 misses on 4 slots
+        torch.ops.asu.asu_hbm_index_lookup_simt(tt, ts, tl, T(np.asarray([[0, 1, 9, 10, 11]], np.int32)), 1)
+    np.testing.assert_array_equal(N(tt), t2s)
+    np.testing.assert_array_equal(N(ts), s2t)
+    np.testing.assert_array_equal(N(tl), lru)
+
+
+# ------------------------------------------------------------------ exact LRU
+
+def _lru_run_and_compare(pools, oracle_pools, steps, check_state_every=1):
+    R = len(oracle_pools)
+    for i, q in enumerate(steps):
+        out = pools.step(T(q))
+        slot, hit, inst = N(out.slot), N(out.hit), N(out.install)
+        ev, evn = N(out.evicted), N(out.evicted_count)
+        for r in range(R):
+            res = oracle_pools[r].step(q[r])
+            np.testing.assert_array_equal(slot[r], res.slot, err_msg=f"step {i} req {r} slot")
+            np.testing.assert_array_equal(hit[r], res.hit, err_msg=f"step {i} req {r} hit")
+            np.testing.assert_array_equal(inst[r], res.install, err_msg=f"step {i} req {r} install")
+            assert evn[r] == len(res.evicted)
+            np.testing.assert_array_equal(ev[r, : evn[r]], res.evicted, err_msg=f"step {i} req {r} evicted")
+        if check_state_every and (i % check_state_every == 0 or i == len(steps) - 1):
+            t2s, s2t, order, stack, count = (N(x) for x in (pools.token_to_slot, pools.slot_to_token,
+                                                             pools.lru_order, pools.free_stack, pools.free_count))
+            for r in range(R):
+                et2s, es2t, eorder, estack, ecount = oracle_pools[r].export_state(pools.key_space)
+                assert count[r] == ecount
+                np.testing.assert_array_equal(t2s[r], et2s)
+                np.testing.assert_array_equal(s2t[r], es2t)
+                nres = pools.slot_count - ecount
+                np.testing.assert_array_equal(order[r, :nres], eorder[:nres])
+                np.testing.assert_array_equal(stack[r, :ecount], estack[:ecount])
+    pools.check_status()
+
+
+@pytest.mark.parametrize("name", ["a", "b", "c", "d"])
+def test_lru_matches_reference_simulator_golden(golden, name):
+    from asu_ascend_b200.lru import LruSlotPools
+
+    g = golden("lru_small")
+    slots, target, key_space, n, q = (int(v) for v in g[f"{name}_meta"])
+    pools = LruSlotPools(1, key_space, slots, target, q, device=DEV)
+    for s in range(n):
+        out = pools.step(T(g[f"{name}_query"][s][None, :]))
+        np.testing.assert_array_equal(N(out.slot)[0], g[f"{name}_slot"][s])
+        np.testing.assert_array_equal(N(out.hit)[0], g[f"{name}_hit"][s])
+        np.testing.assert_array_equal(N(out.install)[0], g[f"{name}_install"][s])
+        k = int(g[f"{name}_evicted_n"][s])
+        assert int(N(out.evicted_count)[0]) == k
+        np.testing.assert_array_equal(N(out.evicted)[0][:k], g[f"{name}_evicted"][s][:k])
+    cnt = int(N(pools.free_count)[0])
+    np.testing.assert_array_equal(N(pools.lru_order)[0][: slots - cnt], g[f"{name}_final_order"])
+    np.testing.assert_array_equal(N(pools.free_stack)[0][:cnt], g[f"{name}_final_free"])
+
+
+def test_lru_matches_reference_on_c0_full_trace(golden):
+    """1 request, 131072 keys, 16384 slots, target 2048, 256 steps x 2048 ids: per-step digests."""
+    from asu_ascend_b200.lru import LruSlotPools
+    from asu_ascend_b200.workloads import LocalityTrace
+
+    g = golden("lru_c0")
+    tr = LocalityTrace(1, 131072, topk=2048, reuse=0.7, zipf_s=1.1, seed=0)
+    steps = [tr.step() for _ in range(256)]
+    pools = LruSlotPools(1, 131072, 16384, 2048, 2048, device=DEV)
+    for s, q in enumerate(steps):
+        out = pools.step(T(q))
+        k = int(N(out.evicted_count)[0])
+        d = digest(q[0], N(out.slot)[0], N(out.hit)[0], N(out.install)[0], N(out.evicted)[0][:k])
+        assert d == str(g["step_digest"][s]), f"step {s}"
+    cnt = int(N(pools.free_count)[0])
+    order = N(pools.lru_order)[0][: 16384 - cnt]
+    keys = N(pools.slot_to_token)[0][order]
+    assert digest(order, keys, N(pools.free_stack)[0][:cnt]) == str(g["final_digest"][0])
+
+
+def test_lru_many_requests_against_oracle():
+    """16 independent requests (one pool each) with duplicates and shortages, full state compared."""
+    from asu_ascend_b200.lru import LruSlotPools
+
+    rng = np.random.Generator(np.random.PCG64(11))
+    R, K, S, Q, tgt = 16, 3000, 300, 160, 64
+    pools = LruSlotPools(R, K, S, tgt, Q, device=DEV)
+    oracle = [O.LruPool(S, tgt) for _ in range(R)]
+    steps = []
+    hot = rng.integers(0, K, (R, 400))
+    for _ in range(30):
+        q = np.empty((R, Q), np.int32)
+        for r in range(R):
+            q[r] = np.where(rng.random(Q) < 0.7, rng.choice(hot[r], Q), rng.integers(0, K, Q))
+        steps.append(q)
+    _lru_run_and_compare(pools, oracle, steps, check_state_every=5)
+
+
+def test_lru_c2_shape_against_oracle():
+    """128 requests, 128K keys, 8192 slots, target 2048, top-k 2048 with c0 locality: 6 steps."""
+    from asu_ascend_b200.lru import LruSlotPools
+    from asu_ascend_b200.workloads import LocalityTrace
+
+    R = 128
+    tr = LocalityTrace(R, 131072, topk=2048, seed=42)
+    steps = [tr.step() for _ in range(6)]
+    pools = LruSlotPools(R, 131072, 8192, 2048, 2048, device=DEV)
+    oracle = [O.LruPool(8192, 2048) for _ in range(R)]
+    _lru_run_and_compare(pools, oracle, steps, check_state_every=0)
+
+
+def test_lru_invalid_keys_and_shortage_status():
+    from asu_ascend_b200._lib import AsuError
+    from asu_ascend_b200.lru import LruSlotPools
+
+    pools = LruSlotPools(1, 10, 2, 0, 4, device=DEV)
+    out = pools.step(T(np.array([[1, 2, 3, 1]], np.int32)))
+    assert N(out.slot)[0].tolist() == [0, 1, -1, 0]
+    assert N(out.hit)[0].tolist() == [False, False, False, True]
+    pools.check_status()  # shortage alone is not an error
+    assert pools.totals() == {"hits": 1, "misses": 3, "installs": 2, "shortages": 1, "evictions": 0}
+    pools.step(T(np.array([[1, 12, -4, 2]], np.int32)))
+    with pytest.raises(AsuError, match="BAD_QUERY"):
+        pools.check_status()
+
+
+# ------------------------------------------------------------------ swap-in
+
+@pytest.mark.parametrize("row_bytes,R,S,Q", [(656, 16, 512, 256), (41984, 4, 16, 8)])
+def test_swapin_bytes_exact(row_bytes, R, S, Q):
+    from asu_ascend_b200.host_pool import HostRowPool, check_status
+    from asu_ascend_b200.lru import LruSlotPools
+    from asu_ascend_b200.workloads import LocalityTrace, record_addresses
+
+    K = 4096
+    pool = HostRowPool(rows=1000, row_bytes=row_bytes)
+    pool.fill_random(7)
+    rec = record_addresses(R, K, pool.rows)
+    tr = LocalityTrace(R, K, topk=Q, seed=3)
+    lru = LruSlotPools(R, K, S, Q // 4, Q, device=DEV)
+    slot_pool = torch.zeros((R, S, row_bytes), dtype=torch.uint8, device=DEV)
+    expect = np.zeros((R, S, row_bytes), np.uint8)
+    trec = T(rec)
+    status = torch.zeros(R, dtype=torch.int32, device=DEV)
+    for _ in range(5):
+        q = tr.step()
+        tq = T(q)
+        out = lru.step(tq)
+        pool.swapin(trec, tq, out.slot, out.install, slot_pool, status=status)
+        expect = O.swapin(pool.array, rec, q, N(out.slot), N(out.install), expect)
+        np.testing.assert_array_equal(N(slot_pool), expect)
+    check_status(status, "swapin")
+    pool.close()
+
+
+# ------------------------------------------------------------------ resolver
+
+def test_resolver_reference_unit_vectors():
+    """patch/0001 tests/ut/ops/test_asu_kv_resolver.py (patch lines 672-765) through the torch op."""
+    f = torch.ops._C_ascend.npu_asu_resolve_kv_slots_single_req
+    kv0 = torch.arange(16, dtype=torch.float32).reshape(8, 2).to(DEV)
+    kv1 = torch.arange(24, dtype=torch.float32).reshape(8, 3).to(DEV)
+    m0 = torch.full((4, 2), -1.0, device=DEV)
+    m1 = torch.full((4, 3), -1.0, device=DEV)
+    ts = torch.tensor([0, 0, 0, 0, 2, 2], dtype=torch.int32, device=DEV)
+    rec = torch.tensor([0, 4, 0, 0, -1, -1], dtype=torch.int64, device=DEV)
+    hs = torch.full((6,), -1, dtype=torch.int32, device=DEV)
+    own = torch.full((4,), -1, dtype=torch.int32, device=DEV)
+    stack = torch.tensor([0, 1, 2, 3], dtype=torch.int64, device=DEV)
+    cnt = torch.tensor(4, dtype=torch.int32, device=DEV)
+    bt = torch.tensor([2, 0, 3], dtype=torch.int64, device=DEV)
+    out = f(torch.tensor([[[1, 1, 5]]], dtype=torch.int64, device=DEV), 6, 4, ts, rec, hs, own, stack, cnt, bt,
+            kv0, kv1, m0, m1, 2)
+    assert out.tolist() == [[[3, 3, 2]]]
+    assert cnt.item() == 2
+    assert ts.tolist() == [0, 1, 0, 0, 2, 1]
+    assert hs.tolist() == [-1, 3, -1, -1, -1, 2]
+    assert own.tolist() == [-1, -1, 5, 1]
+    assert torch.equal(m0[3], kv0[4]) and torch.equal(m1[3], kv1[4])
+    assert torch.equal(m0[2], kv0[7]) and torch.equal(m1[2], kv1[7])
+
+    # second case: a resident token reuses its slot without consuming the stack
+    kv0 = torch.arange(12, dtype=torch.float32).reshape(6, 2).to(DEV)
+    kv1 = torch.arange(18, dtype=torch.float32).reshape(6, 3).to(DEV)
+    m0 = torch.full((3, 2), -1.0, device=DEV)
+    m1 = torch.full((3, 3), -1.0, device=DEV)
+    m0[1] = torch.tensor([101.0, 102.0], device=DEV)
+    m1[1] = torch.tensor([201.0, 202.0, 203.0], device=DEV)
+    ts = torch.tensor([0, 0, 1], dtype=torch.int32, device=DEV)
+    hs = torch.tensor([-1, -1, 1], dtype=torch.int32, device=DEV)
+    own = torch.tensor([-1, 2, -1], dtype=torch.int32, device=DEV)
+    cnt = torch.tensor(2, dtype=torch.int32, device=DEV)
+    out = f(torch.tensor([[2]], dtype=torch.int32, device=DEV), 3, 3, ts,
+            torch.tensor([0, 1, 2], dtype=torch.int32, device=DEV), hs, own,
+            torch.tensor([0, 2, -1], dtype=torch.int32, device=DEV), cnt,
+            torch.tensor([0, 1], dtype=torch.int32, device=DEV), kv0, kv1, m0, m1, 2)
+    assert out.tolist() == [[1]]
+    assert cnt.item() == 2
+    assert m0[1].tolist() == [101.0, 102.0] and m1[1].tolist() == [201.0, 202.0, 203.0]
+
+
+def test_resolver_matches_golden(golden):
+    g = golden("resolver")
+    max_seq, slots, bs, actual, prefix = (int(v) for v in g["meta"])
+    ts, rec, hs, own, stack, cnt = O.reset_state(max_seq, slots, bs, actual, prefix, g["block_table"])
+    np.testing.assert_array_equal(ts, g["reset_token_state"])
+    kv0 = T(g["kv0"]).view(torch.bfloat16)
+    kv1 = T(g["kv1"]).view(torch.bfloat16)
+    m0 = torch.zeros((slots,) + tuple(kv0.shape[1:]), dtype=torch.bfloat16, device=DEV)
+    m1 = torch.zeros((slots,) + tuple(kv1.shape[1:]), dtype=torch.bfloat16, device=DEV)
+    tts, trec, ths, town, tstack, tcnt, tbt = T(ts), T(rec), T(hs), T(own), T(stack), T(cnt), T(g["block_table"])
+    for s in range(3):
+        out = torch.ops._C_ascend.npu_asu_resolve_kv_slots_single_req(
+            T(g[f"s{s}_topk"]), actual, prefix, tts, trec, ths, town, tstack, tcnt, tbt, kv0, kv1, m0, m1, bs)
+        np.testing.assert_array_equal(N(out), g[f"s{s}_out"])
+        np.testing.assert_array_equal(N(tts), g[f"s{s}_token_state"])
+        np.testing.assert_array_equal(N(ths), g[f"s{s}_hbm_slot"])
+        np.testing.assert_array_equal(N(town), g[f"s{s}_owner"])
+        assert int(N(tcnt)[0]) == int(g[f"s{s}_count"][0])
+        assert digest(N(m0.view(torch.int16)), N(m1.view(torch.int16))) == str(g[f"s{s}_kv_digest"][0])
+
+
+def test_resolver_second_resolve_is_idempotent():
+    """patch/0004 invariant: resolving the same top-k twice consumes no free slots."""
+    rng = np.random.Generator(np.random.PCG64(8))
+    max_seq, slots, bs, actual, prefix = 8192, 4096, 64, 6000, 5990
+    bt = rng.permutation(200)[:128].astype(np.int32)
+    ts, rec, hs, own, stack, cnt = O.reset_state(max_seq, slots, bs, actual, prefix, bt)
+    kv0 = torch.randn(200 * bs, 1, 512, device=DEV).to(torch.bfloat16)
+    kv1 = torch.randn(200 * bs, 1, 64, device=DEV).to(torch.bfloat16)
+    m0 = torch.zeros(slots, 1, 512, dtype=torch.bfloat16, device=DEV)
+    m1 = torch.zeros(slots, 1, 64, dtype=torch.bfloat16, device=DEV)
+    tts, trec, ths, town, tstack, tcnt = T(ts), T(rec), T(hs), T(own), T(stack), T(cnt)
+    topk = T(rng.integers(0, actual, (1, 2048)).astype(np.int32))
+    f = torch.ops.asu.npu_asu_resolve_kv_slots_single_req
+    first = f(topk, actual, prefix, tts, trec, ths, town, tstack, tcnt, T(bt), kv0, kv1, m0, m1, bs)
+    c1 = int(tcnt.item())
+    second = f(topk, actual, prefix, tts, trec, ths, town, tstack, tcnt, T(bt), kv0, kv1, m0, m1, bs)
+    assert int(tcnt.item()) == c1
+    assert torch.equal(first, second)
+    topk_np, res_np = N(topk)[0], N(first)[0]
+    for tok, slot in list(zip(topk_np, res_np))[:64]:
+        src = rec[tok] if ts[tok] == 0 else bt[tok // bs] * bs + tok % bs
+        assert torch.equal(m0[slot], kv0[src]) and torch.equal(m1[slot], kv1[src])
+
+
+def test_resolver_errors_are_reported():
+    from asu_ascend_b200._lib import AsuError
+
+    f = torch.ops.asu.npu_asu_resolve_kv_slots_single_req
+    z = lambda n: torch.zeros(n, dtype=torch.int32, device=DEV)  # noqa: E731
+    kv = torch.zeros(4, 2, device=DEV)
+    m = torch.zeros(1, 2, device=DEV)
+    with pytest.raises(AsuError, match="FREE_EXHAUSTED"):
+        f(torch.tensor([0, 1], dtype=torch.int32, device=DEV), 4, 4, z(4), z(4), z(4) - 1, z(1) - 1, z(1),
+          torch.ones(1, dtype=torch.int32, device=DEV), z(2), kv, kv, m, m, 2)
+    with pytest.raises(AsuError, match="BAD_QUERY"):
+        f(torch.tensor([5], dtype=torch.int32, device=DEV), 4, 4, z(4), z(4), z(4) - 1, z(1) - 1, z(1),
+          torch.ones(1, dtype=torch.int32, device=DEV), z(2), kv, kv, m, m, 2)
