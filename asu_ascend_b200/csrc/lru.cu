@@ -12,29 +12,38 @@
 //   free_stack    [R, S]  first free_count entries, top last
 //   free_count    [R]
 //
-// B200 design: one CTA of 1024 threads per request row, everything in one launch.
-//  1. Eviction needs no sort: the victims are the head of lru_order.  Each is unmapped and
-//     pushed on the free stack in order (evicted keys are written in eviction order).
-//  2. Lookup: queries are thread-contiguous; the first occurrence of each missing key is
-//     found with an atomicMin claim (INT32_MIN + position) on its token_to_slot entry; a
-//     block scan ranks first occurrences in query order and rank k pops
-//     free_stack[free - 1 - k].  Later duplicates read the installed slot (serially they
-//     are hits).  Every touch records its position with a shared-memory atomicMax on
-//     last_pos[slot], so the last occurrence of a slot is known.
-//  3. The new LRU order is [untouched residents in old order] ++ [touched slots ordered by
-//     their last touching position] -- exactly the OrderedDict order after the serial
-//     loop.  Both parts are stable compactions done with two block scans; the remaining
-//     old order was held in registers, so the order row is rewritten in place.
-// Per step and request the kernel reads/writes the order row once (8*S bytes) plus 14
-// bytes per query; no global scratch.
+// B200 design: one CTA of 1024 threads per request row, everything in one launch, with
+// the global round trips taken off the critical path:
+//  * At launch every thread issues its loads together: the free count, the whole order
+//    row (coalesced into shared memory) and the token_to_slot gathers of its queries.
+//  * Eviction needs no sort: the victims are the head of the order row.  They are marked
+//    in shared memory (last_pos = -2), so a query that read a victim's slot before the
+//    eviction landed is classified as a miss -- exactly what the serial order (evict,
+//    then resolve) gives.  Victim unmapping stores happen while the gathers are in flight.
+//  * The first occurrence of each missing key is found in a shared-memory hash table
+//    (atomicMin of the position per key); a block scan ranks first occurrences in query
+//    order and rank k pops the free stack: the victims just pushed (top first), then the
+//    older entries, which were prefetched into shared memory.  Later duplicates read the
+//    installed slot from the hash entry (serially they are hits).
+//  * Every touch records its position in last_pos[slot] (shared-memory atomicMax); the
+//    new order is [untouched residents in old order] ++ [touched slots by last touching
+//    position] -- the OrderedDict order after the serial loop -- built with two block
+//    scans in shared memory and written back with coalesced stores.
+// No global scratch; the row is read once and written once.
 #include "asu_common.cuh"
 
 namespace asu {
 namespace {
 
 constexpr int kThreads = 1024;
+constexpr int32_t kVictim = -2;  // last_pos marker of a slot evicted in this step
+constexpr int32_t kEmptyKey = -1;
 
-enum : uint8_t { kInvalid = 0, kHit = 1, kMiss = 2 };
+enum : uint8_t { kInvalid = 0, kHit = 1, kMiss = 2, kBad = 3 };
+
+__device__ __forceinline__ uint32_t hash_slot(int32_t key, int log2h) {
+    return (static_cast<uint32_t>(key) * 0x9E3779B1u) >> (32 - log2h);
+}
 
 template <int IPT_Q, int IPT_S>
 __global__ void __launch_bounds__(kThreads)
@@ -43,11 +52,19 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
                 int32_t* __restrict__ slot_out, uint8_t* __restrict__ hit_mask, uint8_t* __restrict__ install_mask,
                 int32_t* __restrict__ evicted, uint32_t ev_stride, int32_t* __restrict__ ev_count,
                 int64_t* __restrict__ stats, int32_t* status, uint32_t req_num, uint32_t K, uint32_t S, uint32_t Q,
-                uint32_t target) {
-    extern __shared__ int32_t last_pos[];  // [S]
+                uint32_t target, int log2h) {
+    extern __shared__ int32_t smem[];
+    const uint32_t H = 1u << log2h;
+    int32_t* s_order = smem;           // [S]  old order row, later the new one
+    int32_t* s_last = s_order + S;     // [S]  last touching position, -1 untouched, -2 victim
+    int32_t* s_hkey = s_last + S;      // [H]  hash: key
+    int32_t* s_hpos = s_hkey + H;      // [H]  hash: first position
+    int32_t* s_hval = s_hpos + H;      // [H]  hash: installed slot
+    int32_t* s_stack = s_hval + H;     // [Q]  stack entries below the pushed victims, top first
     __shared__ int scan_buf[33];
     __shared__ int n_hits, n_valid;
     const int tid = threadIdx.x;
+
     for (uint32_t r = blockIdx.x; r < req_num; r += gridDim.x) {
         int32_t* trow = t2s + static_cast<uint64_t>(r) * K;
         int32_t* srow = s2t + static_cast<uint64_t>(r) * S;
@@ -56,113 +73,132 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
         const int32_t* qrow = query + static_cast<uint64_t>(r) * Q;
         int32_t bits = 0;
 
+        // ---- P0: issue every independent load ----
         const int32_t free0 = ld_cg(count + r);
+        for (uint32_t i = tid; i < S; i += kThreads) s_order[i] = ld_cg(orow + i);
+        int32_t key[IPT_Q], g[IPT_Q];
+#pragma unroll
+        for (int j = 0; j < IPT_Q; ++j) {
+            const uint32_t pos = tid * IPT_Q + j;
+            key[j] = -1;
+            g[j] = kNotFound;
+            if (pos < Q) {
+                key[j] = __ldg(qrow + pos);
+                if (static_cast<uint32_t>(key[j]) < K) g[j] = ld_cg(trow + key[j]);
+            }
+        }
+        for (uint32_t i = tid; i < S; i += kThreads) s_last[i] = -1;
+        for (uint32_t i = tid; i < H; i += kThreads) s_hkey[i] = kEmptyKey;
+        if (tid == 0) {
+            n_hits = 0;
+            n_valid = 0;
+        }
         if (free0 < 0 || free0 > static_cast<int32_t>(S)) {  // uniform across the block
             if (tid == 0) flag_status(status, r, ASU_ST_BAD_STATE);
+            __syncthreads();
             continue;
         }
         const int32_t resident0 = static_cast<int32_t>(S) - free0;
         const int32_t tgt = static_cast<int32_t>(target < S ? target : S);
         int32_t E = 0;
         if (free0 < tgt) E = (tgt - free0) < resident0 ? (tgt - free0) : resident0;
+        const int32_t free1 = free0 + E;
+        // prefetch the free-stack entries the pops may reach below the pushed victims
+        const int32_t below = free0 < static_cast<int32_t>(Q) ? free0 : static_cast<int32_t>(Q);
+        for (int32_t i = tid; i < below; i += kThreads) s_stack[i] = ld_cg(krow + (free0 - 1 - i));
+        __syncthreads();
 
-        if (tid == 0) {
-            n_hits = 0;
-            n_valid = 0;
-        }
-        for (uint32_t s = tid; s < S; s += kThreads) last_pos[s] = -1;
-
-        // ---- 1. eviction: victims are lru_order[0, E) ----
+        // ---- P1: eviction of lru_order[0, E) ----
         for (int32_t k = tid; k < E; k += kThreads) {
-            const int32_t v = ld_cg(orow + k);
-            int32_t key = kNotFound;
+            const int32_t v = s_order[k];
+            int32_t vkey = kNotFound;
             if (static_cast<uint32_t>(v) < S) {
-                key = ld_cg(srow + v);
-                if (static_cast<uint32_t>(key) < K) st_cg(trow + key, kNotFound);
+                s_last[v] = kVictim;
+                vkey = ld_cg(srow + v);
+                if (static_cast<uint32_t>(vkey) < K) st_cg(trow + vkey, kNotFound);
                 else bits |= ASU_ST_BAD_STATE;
                 st_cg(srow + v, kNotFound);
                 st_cg(krow + free0 + k, v);
             } else {
                 bits |= ASU_ST_BAD_STATE;
             }
-            if (static_cast<uint32_t>(k) < ev_stride) evicted[static_cast<uint64_t>(r) * ev_stride + k] = key;
+            if (static_cast<uint32_t>(k) < ev_stride) evicted[static_cast<uint64_t>(r) * ev_stride + k] = vkey;
         }
         if (tid == 0) ev_count[r] = E;
-        const int32_t n_rem = resident0 - E;
-        int32_t oldv[IPT_S];
-#pragma unroll
-        for (int j = 0; j < IPT_S; ++j) {
-            const int32_t idx = tid * IPT_S + j;
-            oldv[j] = idx < n_rem ? ld_cg(orow + E + idx) : -1;
-        }
-        const int32_t free1 = free0 + E;
-        __syncthreads();
+        __syncthreads();  // victim marks visible; victim unmapping ordered before any install
 
-        // ---- 2. lookup ----
-        int32_t key[IPT_Q], slot[IPT_Q];
+        // ---- P2: classify; hits record their position, misses enter the hash ----
         uint8_t st[IPT_Q];
+        int32_t hidx[IPT_Q];
         int valid_local = 0;
 #pragma unroll
         for (int j = 0; j < IPT_Q; ++j) {
-            const uint32_t pos = tid * IPT_Q + j;
-            key[j] = -1;
-            slot[j] = kNotFound;
+            const int32_t pos = tid * IPT_Q + j;
             st[j] = kInvalid;
-            if (pos < Q) {
-                key[j] = __ldg(qrow + pos);
-                if (static_cast<uint32_t>(key[j]) < K) {
-                    ++valid_local;
-                    const int32_t v = ld_cg(trow + key[j]);
-                    if (v >= 0 && static_cast<uint32_t>(v) < S) {
-                        st[j] = kHit;
-                        slot[j] = v;
-                    } else if (v == kNotFound) {
-                        st[j] = kMiss;
-                    } else {
-                        bits |= ASU_ST_BAD_STATE;
-                    }
-                } else {
-                    bits |= ASU_ST_BAD_QUERY;
+            hidx[j] = -1;
+            if (static_cast<uint32_t>(pos) >= Q) continue;
+            if (static_cast<uint32_t>(key[j]) >= K) {
+                bits |= ASU_ST_BAD_QUERY;
+                continue;
+            }
+            ++valid_local;
+            const int32_t s = g[j];
+            if (s >= 0 && static_cast<uint32_t>(s) < S && s_last[s] != kVictim) {
+                st[j] = kHit;
+                atomicMax(&s_last[s], pos);
+            } else if (s == kNotFound || (s >= 0 && static_cast<uint32_t>(s) < S)) {
+                st[j] = kMiss;
+                uint32_t h = hash_slot(key[j], log2h);
+                while (true) {  // terminates: at most Q <= H distinct keys
+                    const int32_t old = atomicCAS(&s_hkey[h], kEmptyKey, key[j]);
+                    if (old == kEmptyKey || old == key[j]) break;
+                    h = (h + 1) & (H - 1);
                 }
+                hidx[j] = static_cast<int32_t>(h);
+                if (s_hkey[h] == key[j]) s_hpos[h] = 0x7fffffff;  // benign same-value race
+            } else {
+                st[j] = kBad;
+                bits |= ASU_ST_BAD_STATE;
             }
         }
-        __syncthreads();  // all pre-step values read before any claim lands
-#pragma unroll
-        for (int j = 0; j < IPT_Q; ++j) {
-            const int32_t pos = tid * IPT_Q + j;
-            if (st[j] == kMiss) atomicMin(trow + key[j], kClaimBase + pos);
-            else if (st[j] == kHit) atomicMax(&last_pos[slot[j]], pos);
-        }
         __syncthreads();
+#pragma unroll
+        for (int j = 0; j < IPT_Q; ++j)
+            if (st[j] == kMiss) atomicMin(&s_hpos[hidx[j]], static_cast<int32_t>(tid * IPT_Q + j));
+        __syncthreads();
+
+        // ---- P3: first occurrences pop the stack in query order ----
         int canon[IPT_Q];
         int local = 0;
 #pragma unroll
         for (int j = 0; j < IPT_Q; ++j) {
-            const int32_t pos = tid * IPT_Q + j;
-            canon[j] = st[j] == kMiss && ld_cg(trow + key[j]) == kClaimBase + pos;
+            canon[j] = st[j] == kMiss && s_hpos[hidx[j]] == static_cast<int32_t>(tid * IPT_Q + j);
             local += canon[j];
         }
         int n_canon = 0;
         int rank = block_exclusive_scan(local, scan_buf, &n_canon);
+        int32_t slot[IPT_Q];
         uint8_t inst[IPT_Q];
 #pragma unroll
         for (int j = 0; j < IPT_Q; ++j) {
+            slot[j] = st[j] == kHit ? g[j] : kNotFound;
             inst[j] = 0;
             if (!canon[j]) continue;
             const int32_t pos = tid * IPT_Q + j;
             const int32_t k = rank++;
             int32_t s = kNotFound;
             if (k < free1) {
-                s = ld_cg(krow + (free1 - 1 - k));
+                s = k < E ? s_order[E - 1 - k] : s_stack[k - E];
                 if (static_cast<uint32_t>(s) >= S) {
                     bits |= ASU_ST_BAD_STATE;
                     s = kNotFound;
                 }
             }
-            st_cg(trow + key[j], s);
+            s_hval[hidx[j]] = s;
             if (s >= 0) {
+                st_cg(trow + key[j], s);
                 st_cg(srow + s, key[j]);
-                atomicMax(&last_pos[s], pos);
+                atomicMax(&s_last[s], pos);
                 inst[j] = 1;
             } else {
                 bits |= ASU_ST_SHORTAGE;
@@ -172,17 +208,19 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
         const int32_t n_inst = n_canon < free1 ? n_canon : free1;
         const int32_t free2 = free1 - n_inst;
         __syncthreads();
+
+        // ---- P4: later duplicates of a missing key, outputs ----
         int hits_local = 0;
 #pragma unroll
         for (int j = 0; j < IPT_Q; ++j) {
             const int32_t pos = tid * IPT_Q + j;
             bool hit = st[j] == kHit;
-            if (st[j] == kMiss && !canon[j]) {  // later duplicate of a missing key
-                const int32_t v = ld_cg(trow + key[j]);
+            if (st[j] == kMiss && !canon[j]) {
+                const int32_t v = s_hval[hidx[j]];
                 if (v >= 0) {
                     slot[j] = v;
                     hit = true;
-                    atomicMax(&last_pos[v], pos);
+                    atomicMax(&s_last[v], pos);
                 }
             }
             hits_local += hit;
@@ -197,33 +235,36 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
         if (valid_local) atomicAdd(&n_valid, valid_local);
         __syncthreads();
 
-        // ---- 3. new LRU order ----
-        int keep_local = 0;
+        // ---- P5: new LRU order ----
+        const int32_t n_rem = resident0 - E;
+        int32_t oldv[IPT_S];
         bool keep[IPT_S];
+        int keep_local = 0;
 #pragma unroll
         for (int j = 0; j < IPT_S; ++j) {
-            keep[j] = static_cast<uint32_t>(oldv[j]) < S && last_pos[oldv[j]] == -1;
-            if (tid * IPT_S + j < n_rem && static_cast<uint32_t>(oldv[j]) >= S) bits |= ASU_ST_BAD_STATE;
+            const int32_t idx = tid * IPT_S + j;
+            oldv[j] = idx < n_rem ? s_order[E + idx] : -1;
+            keep[j] = static_cast<uint32_t>(oldv[j]) < S && s_last[oldv[j]] == -1;
+            if (idx < n_rem && static_cast<uint32_t>(oldv[j]) >= S) bits |= ASU_ST_BAD_STATE;
             keep_local += keep[j];
         }
         int n_keep = 0;
         int a = block_exclusive_scan(keep_local, scan_buf, &n_keep);
-        int touched_local = 0;
         bool touched[IPT_Q];
+        int touched_local = 0;
 #pragma unroll
         for (int j = 0; j < IPT_Q; ++j) {
-            const int32_t pos = tid * IPT_Q + j;
-            touched[j] = slot[j] >= 0 && last_pos[slot[j]] == pos;
+            touched[j] = slot[j] >= 0 && s_last[slot[j]] == static_cast<int32_t>(tid * IPT_Q + j);
             touched_local += touched[j];
         }
         int n_touched = 0;
-        int b = block_exclusive_scan(touched_local, scan_buf, &n_touched);
-        // A consistent state has n_keep + n_touched == S - free2 <= S; the bounds guard only
-        // matters for corrupt input (duplicate slots across the maps), which is flagged below.
+        int b = block_exclusive_scan(touched_local, scan_buf, &n_touched);  // its barriers end all s_order reads
+        // A consistent state has n_keep + n_touched == S - free2 <= S; the guards only matter
+        // for corrupt input (duplicate slots across the maps), which is flagged below.
 #pragma unroll
         for (int j = 0; j < IPT_S; ++j) {
             if (keep[j]) {
-                if (a < static_cast<int>(S)) st_cg(orow + a, oldv[j]);
+                if (a < static_cast<int>(S)) s_order[a] = oldv[j];
                 ++a;
             }
         }
@@ -231,9 +272,12 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
         for (int j = 0; j < IPT_Q; ++j) {
             if (touched[j]) {
                 const int o = n_keep + b++;
-                if (o < static_cast<int>(S)) st_cg(orow + o, slot[j]);
+                if (o < static_cast<int>(S)) s_order[o] = slot[j];
             }
         }
+        __syncthreads();
+        const int n_new = min(n_keep + n_touched, static_cast<int>(S));
+        for (int i = tid; i < n_new; i += kThreads) st_cg(orow + i, s_order[i]);
         if (tid == 0) {
             st_cg(count + r, free2);
             if (n_keep + n_touched != static_cast<int>(S) - free2) bits |= ASU_ST_BAD_STATE;
@@ -251,26 +295,49 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
     }
 }
 
+inline uint32_t pow2ceil(uint32_t x) {
+    uint32_t p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+
+// Dynamic shared memory of one launch: order + last_pos rows, the hash table, the stack prefetch.
+inline size_t lru_smem_bytes(uint32_t S, uint32_t Q, int* log2h_out) {
+    uint32_t h = 2 * pow2ceil(Q < 16 ? 16 : Q);
+    size_t bytes = (2ull * S + 3ull * h + Q) * sizeof(int32_t);
+    if (bytes > 200u * 1024u) {  // large S and Q together: load factor up to 1 (still terminates)
+        h /= 2;
+        bytes = (2ull * S + 3ull * h + Q) * sizeof(int32_t);
+    }
+    int l = 0;
+    while ((1u << l) < h) ++l;
+    *log2h_out = l;
+    return bytes;
+}
+
+constexpr size_t kMaxSmem = 227u * 1024u;
+
 template <int IPT_Q, int IPT_S>
 int launch_lru(cudaStream_t s, int32_t* t2s, int32_t* s2t, int32_t* order, int32_t* stack, int32_t* count,
                const int32_t* query, int32_t* slot_out, uint8_t* hit, uint8_t* inst, int32_t* evicted,
                uint32_t ev_stride, int32_t* ev_count, int64_t* stats, int32_t* status, uint32_t R, uint32_t K,
                uint32_t S, uint32_t Q, uint32_t target) {
     static unsigned long long configured = 0;  // one bit per device: the attribute is per context
-    const int smem = static_cast<int>(S * sizeof(int32_t));
+    int log2h = 0;
+    const size_t smem = lru_smem_bytes(S, Q, &log2h);
+    if (smem > kMaxSmem) return ASU_ERR_ARG;
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !((configured >> dev) & 1ull)) {
         cudaError_t e = cudaFuncSetAttribute(lru_step_kernel<IPT_Q, IPT_S>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kThreads * IPT_S * static_cast<int>(sizeof(int32_t)));
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMaxSmem));
         if (e != cudaSuccess) return ASU_ERR_CUDA_BASE + static_cast<int>(e);
         configured |= 1ull << dev;
     }
     const uint32_t grid = R < 65535u ? R : 65535u;
     lru_step_kernel<IPT_Q, IPT_S><<<grid, kThreads, smem, s>>>(t2s, s2t, order, stack, count, query, slot_out, hit,
                                                                  inst, evicted, ev_stride, ev_count, stats, status,
-                                                                 R, K, S, Q, target);
+                                                                 R, K, S, Q, target, log2h);
     return asu_launch_status();
 }
 
@@ -306,7 +373,7 @@ extern "C" int asu_lru_step(void* stream, int32_t* token_to_slot, int32_t* slot_
         (query_count && (!query || !slot_out || !hit_mask || !install_mask)))
         return ASU_ERR_ARG;
     if (key_space == 0 || key_space > 0x7fffffffu || slot_count == 0 || slot_count > 16384u ||
-        query_count > 8192u)
+        query_count > 4096u)
         return ASU_ERR_ARG;
     const uint32_t tgt = free_target < slot_count ? free_target : slot_count;
     if (tgt > 0 && (evicted == nullptr || evicted_stride < tgt)) return ASU_ERR_ARG;
@@ -315,11 +382,7 @@ extern "C" int asu_lru_step(void* stream, int32_t* token_to_slot, int32_t* slot_
         return dispatch_s<2>(slot_count, s, token_to_slot, slot_to_token, lru_order, free_stack, free_count, query,
                              slot_out, hit_mask, install_mask, evicted, evicted_stride, evicted_count, stats, status,
                              req_num, key_space, query_count, free_target);
-    if (query_count <= 4096u)
-        return dispatch_s<4>(slot_count, s, token_to_slot, slot_to_token, lru_order, free_stack, free_count, query,
-                             slot_out, hit_mask, install_mask, evicted, evicted_stride, evicted_count, stats, status,
-                             req_num, key_space, query_count, free_target);
-    return dispatch_s<8>(slot_count, s, token_to_slot, slot_to_token, lru_order, free_stack, free_count, query,
+    return dispatch_s<4>(slot_count, s, token_to_slot, slot_to_token, lru_order, free_stack, free_count, query,
                          slot_out, hit_mask, install_mask, evicted, evicted_stride, evicted_count, stats, status,
                          req_num, key_space, query_count, free_target);
 }

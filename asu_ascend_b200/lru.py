@@ -35,8 +35,8 @@ class LruSlotPools:
                  device: torch.device | str = "cuda"):
         if req_num <= 0 or key_space <= 0 or slot_count <= 0 or query_count <= 0 or free_target < 0:
             raise ValueError("req_num, key_space, slot_count, query_count must be positive; free_target >= 0")
-        if slot_count > 16384 or query_count > 8192 or key_space >= 2**31:
-            raise ValueError("supported: slot_count <= 16384, query_count <= 8192, key_space < 2**31")
+        if slot_count > 16384 or query_count > 4096 or key_space >= 2**31:
+            raise ValueError("supported: slot_count <= 16384, query_count <= 4096, key_space < 2**31")
         self.req_num, self.key_space, self.slot_count = req_num, key_space, slot_count
         self.free_target, self.query_count = min(free_target, slot_count), query_count
         self.device = torch.device(device)

@@ -164,7 +164,7 @@ int asu_hbm_index_lookup_simt_ex(void* stream, int32_t* token_to_slot, int32_t* 
  * Outputs: slot_out [Q], hit_mask [Q] (the simulator's per-query hit), install_mask [Q] (this
  * position took a slot and owes one swap-in), evicted [evicted_stride], evicted_count,
  * stats [ASU_LRU_STAT_COLS] int64 (+=, nullable), status (nullable).
- * Limits: slot_count <= 16384, query_count <= 8192, key_space < 2^31. */
+ * Limits: slot_count <= 16384, query_count <= 4096, key_space < 2^31. */
 int asu_lru_step(void* stream, int32_t* token_to_slot, int32_t* slot_to_token, int32_t* lru_order,
                  int32_t* free_stack, int32_t* free_count, const int32_t* query, int32_t* slot_out,
                  uint8_t* hit_mask, uint8_t* install_mask, int32_t* evicted, uint32_t evicted_stride,
