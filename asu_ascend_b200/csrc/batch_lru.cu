@@ -177,7 +177,10 @@ int launch_batch(cudaStream_t s, int32_t* t2s, int32_t* s2t, int16_t* lru, const
     if (dev < 64 && !((configured >> dev) & 1ull)) {
         cudaError_t e = cudaFuncSetAttribute(batch_lru_kernel<IPT_Q, IPT_S>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-        if (e != cudaSuccess) return ASU_ERR_CUDA_BASE + static_cast<int>(e);
+        if (e != cudaSuccess) {
+            cudaGetLastError();  // leave no error behind for the caller's runtime checks
+            return ASU_ERR_CUDA_BASE + static_cast<int>(e);
+        }
         configured |= 1ull << dev;
     }
     const size_t smem = static_cast<size_t>(Q) * 4 + S;
