@@ -55,9 +55,10 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
                 uint32_t target, int log2h) {
     extern __shared__ int32_t smem[];
     const uint32_t H = 1u << log2h;
-    int32_t* s_order = smem;           // [S]  old order row, later the new one
-    int32_t* s_last = s_order + S;     // [S]  last touching position, -1 untouched, -2 victim
-    int32_t* s_hkey = s_last + S;      // [H]  hash: key
+    const uint32_t Sp = (S + 3) & ~3u;  // row length rounded up to 16 bytes
+    int32_t* s_order = smem;            // [Sp] old order row, later the new one
+    int32_t* s_last = s_order + Sp;     // [Sp] last touching position, -1 untouched, -2 victim
+    int32_t* s_hkey = s_last + Sp;      // [H]  hash: key
     int32_t* s_hpos = s_hkey + H;      // [H]  hash: first position
     int32_t* s_hval = s_hpos + H;      // [H]  hash: installed slot
     int32_t* s_stack = s_hval + H;     // [Q]  stack entries below the pushed victims, top first
@@ -75,7 +76,14 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
 
         // ---- P0: issue every independent load ----
         const int32_t free0 = ld_cg(count + r);
-        for (uint32_t i = tid; i < S; i += kThreads) s_order[i] = ld_cg(orow + i);
+        const bool vec_row = (S % 4 == 0) && (reinterpret_cast<uintptr_t>(orow) % 16 == 0);
+        if (vec_row) {
+            const int4* src = reinterpret_cast<const int4*>(orow);
+            int4* dst = reinterpret_cast<int4*>(s_order);
+            for (uint32_t i = tid; i < S / 4; i += kThreads) dst[i] = __ldcg(src + i);
+        } else {
+            for (uint32_t i = tid; i < S; i += kThreads) s_order[i] = ld_cg(orow + i);
+        }
         int32_t key[IPT_Q], g[IPT_Q];
 #pragma unroll
         for (int j = 0; j < IPT_Q; ++j) {
@@ -87,8 +95,14 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
                 if (static_cast<uint32_t>(key[j]) < K) g[j] = ld_cg(trow + key[j]);
             }
         }
-        for (uint32_t i = tid; i < S; i += kThreads) s_last[i] = -1;
-        for (uint32_t i = tid; i < H; i += kThreads) s_hkey[i] = kEmptyKey;
+        {
+            const int4 m1 = make_int4(-1, -1, -1, -1);
+            // S4 and H are multiples of 4 elements of 16-byte aligned arrays (S4 rounds S up
+            // inside the dynamic allocation, see lru_smem_bytes)
+            const uint32_t S4 = (S + 3) / 4;
+            for (uint32_t i = tid; i < S4; i += kThreads) reinterpret_cast<int4*>(s_last)[i] = m1;
+            for (uint32_t i = tid; i < H / 4; i += kThreads) reinterpret_cast<int4*>(s_hkey)[i] = m1;
+        }
         if (tid == 0) {
             n_hits = 0;
             n_valid = 0;
@@ -236,16 +250,35 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
         __syncthreads();
 
         // ---- P5: new LRU order ----
-        const int32_t n_rem = resident0 - E;
+        // thread t owns s_order[t*IPT_S, (t+1)*IPT_S); entries in [E, resident0) are the
+        // residents that survived the eviction, in LRU order
         int32_t oldv[IPT_S];
         bool keep[IPT_S];
         int keep_local = 0;
+        if (tid * IPT_S < static_cast<int>(Sp)) {
+            if constexpr (IPT_S % 4 == 0) {
+#pragma unroll
+                for (int j = 0; j < IPT_S; j += 4) {
+                    const int4 v4 = reinterpret_cast<const int4*>(s_order)[(tid * IPT_S + j) / 4];
+                    oldv[j] = v4.x;
+                    oldv[j + 1] = v4.y;
+                    oldv[j + 2] = v4.z;
+                    oldv[j + 3] = v4.w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < IPT_S; ++j) oldv[j] = s_order[tid * IPT_S + j];
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < IPT_S; ++j) oldv[j] = -1;
+        }
 #pragma unroll
         for (int j = 0; j < IPT_S; ++j) {
             const int32_t idx = tid * IPT_S + j;
-            oldv[j] = idx < n_rem ? s_order[E + idx] : -1;
-            keep[j] = static_cast<uint32_t>(oldv[j]) < S && s_last[oldv[j]] == -1;
-            if (idx < n_rem && static_cast<uint32_t>(oldv[j]) >= S) bits |= ASU_ST_BAD_STATE;
+            const bool live = idx >= E && idx < resident0;
+            keep[j] = live && static_cast<uint32_t>(oldv[j]) < S && s_last[oldv[j]] == -1;
+            if (live && static_cast<uint32_t>(oldv[j]) >= S) bits |= ASU_ST_BAD_STATE;
             keep_local += keep[j];
         }
         int n_keep = 0;
@@ -277,7 +310,14 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
         }
         __syncthreads();
         const int n_new = min(n_keep + n_touched, static_cast<int>(S));
-        for (int i = tid; i < n_new; i += kThreads) st_cg(orow + i, s_order[i]);
+        if (vec_row) {
+            const int n4 = n_new / 4;
+            for (int i = tid; i < n4; i += kThreads)
+                __stcg(reinterpret_cast<int4*>(orow) + i, reinterpret_cast<const int4*>(s_order)[i]);
+            for (int i = n4 * 4 + tid; i < n_new; i += kThreads) st_cg(orow + i, s_order[i]);
+        } else {
+            for (int i = tid; i < n_new; i += kThreads) st_cg(orow + i, s_order[i]);
+        }
         if (tid == 0) {
             st_cg(count + r, free2);
             if (n_keep + n_touched != static_cast<int>(S) - free2) bits |= ASU_ST_BAD_STATE;
@@ -303,11 +343,12 @@ inline uint32_t pow2ceil(uint32_t x) {
 
 // Dynamic shared memory of one launch: order + last_pos rows, the hash table, the stack prefetch.
 inline size_t lru_smem_bytes(uint32_t S, uint32_t Q, int* log2h_out) {
+    const uint64_t Sp = (S + 3) & ~3u;
     uint32_t h = 2 * pow2ceil(Q < 16 ? 16 : Q);
-    size_t bytes = (2ull * S + 3ull * h + Q) * sizeof(int32_t);
+    size_t bytes = (2ull * Sp + 3ull * h + Q) * sizeof(int32_t);
     if (bytes > 200u * 1024u) {  // large S and Q together: load factor up to 1 (still terminates)
         h /= 2;
-        bytes = (2ull * S + 3ull * h + Q) * sizeof(int32_t);
+        bytes = (2ull * Sp + 3ull * h + Q) * sizeof(int32_t);
     }
     int l = 0;
     while ((1u << l) < h) ++l;
