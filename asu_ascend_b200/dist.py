@@ -1,0 +1,40 @@
+"""Request sharding and end-of-run statistics for multi-GPU runs (one process per GPU).
+
+Requests are independent (each owns its tables, slot pool and host rows), so a job of
+``total`` requests is split into contiguous ranges, one per rank, with no collective on the
+data path.  The only collectives are the end-of-run reductions below (NCCL on GPUs, gloo in
+the CPU tests).
+"""
+
+from __future__ import annotations
+
+import torch
+
+
+def shard_range(total: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous [start, end) of ``total`` requests owned by ``rank`` (sizes differ by at most 1)."""
+    if world <= 0 or not 0 <= rank < world or total < 0:
+        raise ValueError("need world > 0, 0 <= rank < world, total >= 0")
+    base, extra = divmod(total, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def _initialized() -> bool:
+    return torch.distributed.is_available() and torch.distributed.is_initialized()
+
+
+def reduce_stats(stats: torch.Tensor) -> torch.Tensor:
+    """Sum per-rank int64 counters (hits, misses, installs, shortages, evictions) over ranks."""
+    total = stats.reshape(-1, stats.shape[-1]).sum(0).to(torch.int64)
+    if _initialized():
+        torch.distributed.all_reduce(total, op=torch.distributed.ReduceOp.SUM)
+    return total
+
+
+def max_over_ranks(values: list[float], device: torch.device | str = "cpu") -> list[float]:
+    """Element-wise max over ranks (timings are reported as the slowest rank's)."""
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    if _initialized():
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return t.tolist()

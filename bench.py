@@ -208,6 +208,7 @@ def run_b200(args, world: int, rank: int, local_rank: int):
     import asu_ascend_b200
 
     asu_ascend_b200.load()
+    from asu_ascend_b200.dist import max_over_ranks, reduce_stats
     from asu_ascend_b200.host_pool import HostRowPool, check_status
     from asu_ascend_b200.lru import LruSlotPools
     from asu_ascend_b200.workloads import record_addresses
@@ -300,12 +301,8 @@ def run_b200(args, world: int, rank: int, local_rank: int):
     pools.check_status()
     check_status(status, "swapin")
 
-    tot = torch.tensor([sum(step_ms), sum(e2e_ms)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
-        st = pools.stats.sum(0)
-        dist.all_reduce(st)  # end-of-run statistics reduction (NCCL)
-    max_ms, max_e2e_ms = tot.tolist()
+    max_ms, max_e2e_ms = max_over_ranks([sum(step_ms), sum(e2e_ms)], dev)  # slowest rank
+    job_stats = reduce_stats(pools.stats).cpu().tolist()  # end-of-run statistics (NCCL all-reduce)
 
     if rank == 0:
         peaks = load_peaks()
@@ -348,6 +345,7 @@ def run_b200(args, world: int, rank: int, local_rank: int):
             "e2e": {"value": world * R * Q * K_steps / (max_e2e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": R * Q * 4, "d2h_bytes_per_step": R * Q * 5},
             "gpu_launches": 2 * K_steps,
+            "job_stats": dict(zip(LruSlotPools.STAT_NAMES, job_stats)),
             "cpu_baseline": cpu,
             "clocks": clk,
         }

@@ -1,0 +1,72 @@
+"""Multi-rank host logic on CPU: request sharding and the end-of-run statistics reduction
+run as world-size-2 gloo ranks and must equal one process doing all requests."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from asu_ascend_b200.dist import max_over_ranks, reduce_stats, shard_range
+
+
+def test_shard_range_covers_every_request_once():
+    for total in (0, 1, 7, 128, 1024, 1025):
+        for world in (1, 2, 3, 8):
+            seen = []
+            for r in range(world):
+                a, b = shard_range(total, world, r)
+                seen.extend(range(a, b))
+                assert b - a in (total // world, total // world + 1)
+            assert seen == list(range(total))
+    with pytest.raises(ValueError):
+        shard_range(4, 2, 2)
+
+
+def _trace(total_req, steps):
+    from asu_ascend_b200.workloads import LocalityTrace
+
+    tr = LocalityTrace(total_req, 8192, topk=256, seed=77)
+    return np.stack([tr.step() for _ in range(steps)])
+
+
+def _run_rows(trace, rows):
+    from oracle import c_oracle
+
+    pools = c_oracle.LruPools(len(rows), 8192, 1024, 256)
+    for s in range(trace.shape[0]):
+        pools.step_all(trace[s][rows], threads=1, want_outputs=False)
+    st = pools.stats.copy()
+    pools.close()
+    return st
+
+
+def _worker(rank, world, port, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        trace = _trace(6, 5)
+        a, b = shard_range(6, world, rank)
+        st = _run_rows(trace, list(range(a, b)))
+        total = reduce_stats(torch.from_numpy(st))
+        slowest = max_over_ranks([float(rank + 1)])
+        if rank == 0:
+            np.save(out_path, np.concatenate([total.numpy(), np.asarray(slowest, np.int64)]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_match_one_process(tmp_path):
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    out = tmp_path / "stats.npy"
+    mp.spawn(_worker, args=(2, port, str(out)), nprocs=2, join=True)
+    got = np.load(out)
+    expect = _run_rows(_trace(6, 5), list(range(6))).sum(0)
+    np.testing.assert_array_equal(got[:5], expect)
+    assert got[5] == 2  # max over ranks of (rank + 1)
