@@ -18,7 +18,9 @@ LIB_PATH = Path(__file__).resolve().with_name("libasu_b200.so")
 ASU_OK = 0
 ASU_ERR_ARG = -1
 ASU_ERR_ALIGN = -2
+ASU_ERR_NOALLOC_CAPACITY = -3
 ASU_ERR_CUDA_BASE = 1000
+RESOLVER_NOALLOC_MAX_TOPK = 16384
 
 STATUS_BITS = {
     0x01: "BAD_QUERY",
@@ -59,6 +61,8 @@ _SIGS = {
     "asu_kv_resolver_do": [_P, _P, c_int64, _P, _P, _P, _P, _P, _P, c_int64, _P, c_int64, _P, _P, _P, _P, c_int64,
                            c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, _P, _P, _P],
     "asu_kv_resolver_workspace_bytes": [c_int64],
+    "asu_kv_resolver_noalloc": [_P, _P, c_int64, _P, _P, _P, _P, _P, _P, c_int64, _P, c_int64, _P, _P, _P, _P,
+                                c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, _P, _P],
 }
 _RESTYPE = {"asu_status_string": c_char_p, "asu_kv_resolver_workspace_bytes": c_int64}
 

@@ -222,3 +222,80 @@ extern "C" int asu_kv_resolver_do(void* stream, const int32_t* topk, int64_t top
         static_cast<uint8_t*>(kv0_dst), static_cast<uint8_t*>(kv1_dst), kv0_row_bytes, kv1_row_bytes);
     return asu_launch_status();
 }
+
+// ---------------------------------------------------------------------------
+// Resolver entry point that allocates nothing.
+//
+// Some callers cannot allocate device memory when they resolve a layer.  Examples: a serving
+// engine that hands nearly all HBM to its KV-block pool at start-up and forbids cudaMalloc in
+// the decode loop (it could fail there, and it synchronises the device); or a C / FFI host
+// with no caching allocator, which would otherwise pay a cudaMalloc + cudaFree per layer per
+// step.  For them the install list lives in a fixed file-scope device array instead of a
+// caller-provided workspace.
+//
+// * Capacity: ASU_RESOLVER_NOALLOC_MAX_TOPK top-k entries per call (128 KiB of device memory
+//   that every GPU loading this library holds until the process exits).  Larger calls are
+//   rejected with ASU_ERR_NOALLOC_CAPACITY before anything is launched.
+// * Set-up: the first call on a device looks up the array's device address with
+//   cudaGetSymbolAddress (with that device current) and caches it.  Make that first call
+//   before any stream capture on the device.
+// * Sharing: every call on a device uses the same array.  The resolve kernel rewrites the
+//   install count and every entry it later reads, so nothing has to start at zero, but two
+//   calls whose launches overlap on the GPU (different streams, no ordering between them)
+//   race on the array.  Order such calls on one stream.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace {
+
+constexpr int64_t kNoAllocScratchInts = 1 + 2 * static_cast<int64_t>(ASU_RESOLVER_NOALLOC_MAX_TOPK);
+static __device__ __align__(256) int32_t g_noalloc_scratch[kNoAllocScratchInts];
+
+std::mutex g_noalloc_mu;
+int32_t* g_noalloc_addr[64] = {};  // device address of g_noalloc_scratch per device ordinal
+
+int noalloc_scratch(int32_t** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return ASU_ERR_CUDA_BASE + static_cast<int>(e);
+    }
+    if (dev < 0 || dev >= 64) return ASU_ERR_ARG;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_addr[dev] == nullptr) {
+        void* p = nullptr;
+        // The host-side name g_noalloc_scratch is only a stand-in; the kernel needs this address.
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            cudaGetLastError();
+            return e != cudaSuccess ? ASU_ERR_CUDA_BASE + static_cast<int>(e) : ASU_ERR_ARG;
+        }
+        g_noalloc_addr[dev] = static_cast<int32_t*>(p);
+    }
+    *out = g_noalloc_addr[dev];
+    return ASU_OK;
+}
+
+}  // namespace
+
+extern "C" int asu_kv_resolver_noalloc(void* stream, const int32_t* topk, int64_t topk_numel, int32_t* token_state,
+                                       const int32_t* asu_record_addr, int32_t* hbm_slot_of_token,
+                                       int32_t* slot_owner_token, const int32_t* free_slot_stack,
+                                       int32_t* free_slot_count, int64_t free_slot_stack_len,
+                                       const int32_t* block_table, int64_t block_table_len, const void* kv0_src,
+                                       const void* kv1_src, void* kv0_dst, void* kv1_dst, int64_t kv0_row_bytes,
+                                       int64_t kv1_row_bytes, int64_t src_rows, int64_t slot_count,
+                                       int64_t max_seq_len, int64_t actual_seq_len, int64_t block_size,
+                                       int32_t* resolved, int32_t* status) {
+    if (topk_numel > ASU_RESOLVER_NOALLOC_MAX_TOPK) return ASU_ERR_NOALLOC_CAPACITY;
+    if (topk_numel == 0) return ASU_OK;
+    int32_t* scratch = nullptr;
+    const int rc = noalloc_scratch(&scratch);
+    if (rc != ASU_OK) return rc;
+    return asu_kv_resolver_do(stream, topk, topk_numel, token_state, asu_record_addr, hbm_slot_of_token,
+                              slot_owner_token, free_slot_stack, free_slot_count, free_slot_stack_len, block_table,
+                              block_table_len, kv0_src, kv1_src, kv0_dst, kv1_dst, kv0_row_bytes, kv1_row_bytes,
+                              src_rows, slot_count, max_seq_len, actual_seq_len, block_size, resolved, scratch,
+                              status);
+}

@@ -212,6 +212,25 @@ int asu_kv_resolver_do(void* stream, const int32_t* topk, int64_t topk_numel, in
 
 int64_t asu_kv_resolver_workspace_bytes(int64_t topk_numel);
 
+/* No counterpart in the reference.  The same resolver as asu_kv_resolver_do, for callers that
+ * cannot allocate device memory while resolving (an engine whose HBM is pre-reserved for its
+ * KV-block pool and that forbids cudaMalloc in the decode loop; a C / FFI host without a
+ * caching allocator): the install-list scratch is a fixed device array inside the library,
+ * ASU_RESOLVER_NOALLOC_MAX_TOPK entries (128 KiB per GPU that loads the library, held until
+ * exit).  Larger topk_numel returns ASU_ERR_NOALLOC_CAPACITY and launches nothing.  The first
+ * call on a device looks up the array's device address; make it before any stream capture.
+ * All calls on a device share the array: calls whose launches overlap on the GPU race, so
+ * order them on one stream.  Allocates nothing (no cudaMalloc / cudaFree). */
+#define ASU_RESOLVER_NOALLOC_MAX_TOPK 16384
+#define ASU_ERR_NOALLOC_CAPACITY (-3) /* topk_numel above ASU_RESOLVER_NOALLOC_MAX_TOPK */
+int asu_kv_resolver_noalloc(void* stream, const int32_t* topk, int64_t topk_numel, int32_t* token_state,
+                            const int32_t* asu_record_addr, int32_t* hbm_slot_of_token, int32_t* slot_owner_token,
+                            const int32_t* free_slot_stack, int32_t* free_slot_count, int64_t free_slot_stack_len,
+                            const int32_t* block_table, int64_t block_table_len, const void* kv0_src,
+                            const void* kv1_src, void* kv0_dst, void* kv1_dst, int64_t kv0_row_bytes,
+                            int64_t kv1_row_bytes, int64_t src_rows, int64_t slot_count, int64_t max_seq_len,
+                            int64_t actual_seq_len, int64_t block_size, int32_t* resolved, int32_t* status);
+
 #ifdef __cplusplus
 }
 #endif
