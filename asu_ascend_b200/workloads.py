@@ -132,15 +132,93 @@ class UniformReuseTrace:
         return rows
 
 
-def record_addresses(req_num: int, key_space: int, pool_rows: int, salt: int = 0x9E3779B1) -> np.ndarray:
+RECORD_SALT = 2654435761  # odd 32-bit multiplier
+RECORD_OFFSET = 0x7F4A7C15
+
+
+def record_addresses(req_num: int, key_space: int, pool_rows: int) -> np.ndarray:
     """[req_num, key_space] int32 row index of each (request, key) record in the host pool.
 
-    A multiplicative hash scatters records over a pool of ``pool_rows`` rows so
-    that a bounded pinned pool can stand in for a full per-token backing store
-    (several keys may share a row; every check uses the same table).
+    A multiplicative hash scatters records over a pool of ``pool_rows`` rows so that a bounded
+    pinned pool can stand in for a full per-token backing store (several keys may share a
+    row; every check uses the same table).  The product stays below 2**63 for
+    req_num * key_space < 2**31, so torch on the GPU computes the same values
+    (record_addresses_torch).
     """
-    r = np.arange(req_num, dtype=np.uint64)[:, None]
-    k = np.arange(key_space, dtype=np.uint64)[None, :]
-    h = (r * np.uint64(key_space) + k) * np.uint64(salt) + np.uint64(0x7F4A7C15)
-    h ^= h >> np.uint64(29)
-    return (h % np.uint64(pool_rows)).astype(np.int32)
+    r = np.arange(req_num, dtype=np.int64)[:, None]
+    k = np.arange(key_space, dtype=np.int64)[None, :]
+    return (((r * key_space + k) * RECORD_SALT + RECORD_OFFSET) % pool_rows).astype(np.int32)
+
+
+def record_addresses_torch(req_num: int, key_space: int, pool_rows: int, device):
+    """record_addresses computed on ``device`` (same values), for tables too large for host RAM."""
+    import torch
+
+    out = torch.empty((req_num, key_space), dtype=torch.int32, device=device)
+    k = torch.arange(key_space, dtype=torch.int64, device=device)
+    for r in range(req_num):
+        out[r] = ((r * key_space + k) * RECORD_SALT + RECORD_OFFSET).remainder(pool_rows).to(torch.int32)
+    return out
+
+
+class FastLocalityTrace:
+    """Vectorised reuse + Zipf (or uniform) trace for large request counts.
+
+    Same recipe as LocalityTrace -- keep ``reuse`` of the previous ids, draw the rest by
+    Zipf(s) with the CDF method (uniform when ``zipf_s`` is None), distinct within a row, in
+    draw order -- but one random stream serves all rows and every draw column is one vector
+    operation over the rows, so its ids differ from LocalityTrace's.  Used by the
+    multi-layer and stress benchmarks, which need hundreds of rows per step.
+    """
+
+    def __init__(self, req_num: int, key_space: int, topk: int = 2048, reuse: float = 0.7,
+                 zipf_s: float | None = 1.1, seed: int = 0):
+        self.req_num, self.key_space, self.topk = req_num, key_space, topk
+        self.n_reuse = int(round(topk * reuse))
+        self.rng = np.random.Generator(np.random.PCG64(seed))
+        self.cdf = zipf_cdf(key_space, zipf_s) if zipf_s else None
+        self.prev: np.ndarray | None = None
+
+    def _draw(self, shape) -> np.ndarray:
+        if self.cdf is None:
+            return self.rng.integers(0, self.key_space, shape)
+        u = self.rng.random(shape) * self.cdf[-1]
+        return np.minimum(np.searchsorted(self.cdf, u, side="left"), self.key_space - 1)
+
+    def step(self) -> np.ndarray:
+        R, K = self.req_num, self.key_space
+        rows = np.arange(R)
+        if self.prev is None:
+            keep = np.zeros((R, 0), np.int64)
+        else:
+            perm = np.argsort(self.rng.random(self.prev.shape), axis=1)[:, : self.n_reuse]
+            keep = np.take_along_axis(self.prev, perm, axis=1).astype(np.int64)
+        need = self.topk - keep.shape[1]
+        taken = np.zeros((R, K), bool)
+        taken[rows[:, None], keep] = True
+        fresh = np.empty((R, need), np.int64)
+        filled = np.zeros(R, np.int64)
+        rounds = 0
+        while True:
+            pend = np.flatnonzero(filled < need)
+            if pend.size == 0:
+                break
+            rounds += 1
+            uniform = self.cdf is None or rounds > 16  # heavy head: finish with uniform draws
+            cand = (self.rng.integers(0, K, (pend.size, 2 * need)) if uniform
+                    else self._draw((pend.size, 2 * need)))
+            for c in range(cand.shape[1]):
+                v = cand[:, c]
+                ok = (~taken[pend, v]) & (filled[pend] < need)
+                if not ok.any():
+                    if (filled[pend] >= need).all():
+                        break
+                    continue
+                rr, vv = pend[ok], v[ok]
+                taken[rr, vv] = True
+                fresh[rr, filled[rr]] = vv
+                filled[rr] += 1
+        out = np.concatenate([keep, fresh], axis=1)
+        out = np.take_along_axis(out, np.argsort(self.rng.random(out.shape), axis=1), axis=1)
+        self.prev = out.astype(np.int32)
+        return self.prev

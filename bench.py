@@ -1,24 +1,34 @@
 #!/usr/bin/env python
-"""Benchmark of the KV-resolver hot path on B200: one step = one decode-layer resolve for a
-batch of requests -- exact-LRU maintain + lookup (one kernel) followed by the swap-in
-gather of every missed 656-byte KV row from pinned, mapped host memory into the HBM slot
-pool (one kernel).
+"""Benchmark of the KV-resolver hot path on B200.
 
-    python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference]
+    python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference] [--workload NAME]
 
-Workload (per GPU; requests are sharded, so N GPUs run N x 128 independent requests, weak
-scaling, no collective on the data path): 128 requests, 128K-token context, top-k 2048
-per step with reuse + Zipf locality (70% of the previous step's ids kept, 30% Zipf(1.1)
-draws), 8192 HBM slots per request, LRU free target 2048, KV rows of 656 B (512 fp8 +
-64 bf16 + 16 B scales, random bytes) in a 2^20-row pinned host pool.  Inputs are
-synthetic and seeded.  The pools are first filled by `--prefill` untimed steps so the
-timed steps run at the steady-state miss rate (~13%).
+Default workload `resolver` (the configuration the headline metric is quoted on): one step is
+one decode-layer resolve for 128 requests per GPU --
+  * exact-LRU maintain + lookup (one kernel);
+  * the swap-in gather of every missed 656-byte KV row (512 fp8 + 64 bf16 + 16 B scales,
+    random bytes) from pinned, mapped host memory into the HBM slot pool (one kernel).
+Each request has a 128K-token context, a top-k of 2048 per step with reuse + Zipf locality
+(70% of the previous step's ids kept, 30% Zipf(1.1) draws), 8192 HBM slots and an LRU free
+target of 2048.  Requests are sharded over GPUs: N GPUs run N x 128 independent requests
+(weak scaling) with no collective on the data path.  The pools are first filled by
+`--prefill` untimed steps so the timed steps run at the steady-state miss rate.
 
-Prints one JSON line (rank 0).  `value` is resolved KV indices/s for the whole job with
-inputs resident in HBM; `e2e` is the same through the public API with the step's top-k
-copied from pinned host memory and the slot ids + hit mask copied back inside the timed
-region.  `--impl reference` times the CPU restatement of the reference algorithm on all
-host cores (the reference's own implementation is Python / AscendC and cannot run here).
+Other workloads (`--workload`):
+  lru1          1 request, 128K keys, 16384 slots, target 2048, LRU maintain + lookup only
+  lookup        64 x 2048 queries gathered from 64 x 128K tables (4096 resident), hit mask
+  multilayer    1024 requests split over the GPUs (strong scaling), 4 layers per decode
+                step with independent top-k, one 8192-slot pool per request shared by them
+  stress        128 requests, 1M-token context, top-k 2048, 20% reuse + uniform draws
+  stress-block  the stress context in 64-token blocks: top-k 32 blocks, 128 block slots,
+                41,984-byte rows
+All inputs are synthetic and seeded.
+
+Prints one JSON line (rank 0).  `value` is resolved indices/s for the whole job with inputs
+resident in HBM; `e2e` is the same through the public API with the step's top-k copied from
+pinned host memory and the slot ids + hit mask copied back inside the timed region.
+`--impl reference` times the CPU restatement of the reference algorithm on all host cores
+(the reference's own implementation is a Python simulator / AscendC kernels).
 """
 
 from __future__ import annotations
@@ -31,6 +41,7 @@ import subprocess
 import sys
 import threading
 import time
+from dataclasses import dataclass
 from datetime import timedelta
 from pathlib import Path
 
@@ -39,14 +50,47 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-R, K, S, Q, TARGET, ROW = 128, 131072, 8192, 2048, 2048, 656
 POOL_ROWS = 1 << 20
-# From the ncu captures summarised in profiles/ (first timed step of this workload):
-SWAPIN_PCIE_READ_BYTES_PER_LAUNCH = 52.49e9 * 714.4e-6   # pcie__read_bytes.sum.per_second x duration
-SWAPIN_NCU_INSTALLS = 31.0e6 / ROW                        # rows swapped in by that launch (~31 MB)
-LRU_DRAM_BYTES_PER_LAUNCH = 22.05e6 + 0.055e6             # dram__bytes_read.sum + dram__bytes_write.sum
-METRIC = "resolved KV indices/sec (lookup + LRU maintain + swap-in gather)"
 UNIT = "indices/s"
+METRIC = "resolved KV indices/sec (lookup + LRU maintain + swap-in gather)"
+# Published reference number for the pure lookup: 50 req x 2048 queries in ~350 us on
+# Ascend 910B (docs/archive/hbm_kvcache_lookup_recommendations.md:32) = 2.93e8 indices/s.
+REF_LOOKUP_IDX_PER_S = 50 * 2048 / 350e-6
+# From the ncu captures summarised in profiles/ (first timed step of the resolver workload):
+SWAPIN_PCIE_READ_BYTES_PER_LAUNCH = 52.49e9 * 714.4e-6   # pcie__read_bytes.sum.per_second x duration
+SWAPIN_NCU_INSTALLS = 31.0e6 / 656                        # rows swapped in by that launch (~31 MB)
+LRU_DRAM_BYTES_PER_LAUNCH = 22.05e6 + 0.055e6             # dram__bytes_read.sum + dram__bytes_write.sum
+
+
+@dataclass
+class ResolverCfg:
+    name: str
+    req: int            # requests per GPU (weak) or in the whole job (strong)
+    keys: int           # logical positions per layer
+    slots: int
+    topk: int
+    target: int
+    row: int
+    layers: int = 1
+    reuse: float = 0.7
+    zipf: float | None = 1.1
+    strong: bool = False
+    fast_trace: bool = False
+
+    def describe(self) -> str:
+        return (f"{self.name}: {self.req} req{'' if self.strong else '/GPU'} x top-k {self.topk} x {self.layers} "
+                f"layer(s), {self.keys} keys, {self.slots} slots/req, LRU target {self.target}, {self.row} B rows "
+                f"from a pinned host pool")
+
+
+RESOLVER_WORKLOADS = {
+    "resolver": ResolverCfg("resolver", 128, 131072, 8192, 2048, 2048, 656),
+    "multilayer": ResolverCfg("multilayer", 1024, 131072, 8192, 2048, 2048, 656, layers=4, strong=True,
+                              fast_trace=True),
+    "stress": ResolverCfg("stress", 128, 1 << 20, 8192, 2048, 2048, 656, reuse=0.2, zipf=None, fast_trace=True),
+    "stress-block": ResolverCfg("stress-block", 128, (1 << 20) // 64, 128, 32, 32, 41984, reuse=0.2, zipf=None,
+                                fast_trace=True),
+}
 
 
 def parse_args():
@@ -56,6 +100,8 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--prefill", type=int, default=8)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--workload", choices=("resolver", "lru1", "lookup", "multilayer", "stress", "stress-block"),
+                   default="resolver")
     p.add_argument("--seed", type=int, default=2026)
     p.add_argument("--cpu-sample-s", type=float, default=12.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -69,12 +115,13 @@ def load_peaks():
         return {}
 
 
-def config_dict(world: int) -> dict:
-    return {"workload": f"resolver: {R} req/GPU x top-k {Q}, 128K context, {S} slots/req, LRU target {TARGET}, "
-                        f"{ROW} B rows from a pinned host pool ({POOL_ROWS} rows)",
-            "requests_per_gpu": R, "global_batch": R * world, "topk": Q, "context": K, "slots_per_request": S,
-            "free_target": TARGET, "row_bytes": ROW, "locality": "70% reuse + 30% zipf(1.1)",
-            "l2": "flushed before every timed step (256 MiB write, then 256 MiB read so no dirty lines remain)", "parallelism": f"request-sharded x{world}"}
+def base_line(world, steps, warmup, ms, value, config, scaling="weak", vs=None):
+    return {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": scaling, "vs_baseline": vs, "dtype": "int32",
+            "data": "synthetic", "config": config}
+
+
+L2_NOTE = "flushed before every timed step (256 MiB write, then 256 MiB read so no dirty lines remain)"
 
 
 # ------------------------------------------------------------------ clocks
@@ -131,60 +178,99 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            return int(vis.split(",")[local_rank])
+        except (ValueError, IndexError):
+            return local_rank
+    return local_rank
+
+
+# ------------------------------------------------------------------ traces
+
+def make_trace(cfg: ResolverCfg, req: int, seed: int, n_steps: int) -> np.ndarray:
+    """[n_steps, layers, req, topk] int32 logical ids (per layer, before folding the layer in)."""
+    from asu_ascend_b200.workloads import FastLocalityTrace, LocalityTrace
+
+    out = np.empty((n_steps, cfg.layers, req, cfg.topk), np.int32)
+    for layer in range(cfg.layers):
+        s = seed + 7919 * layer
+        if cfg.fast_trace:
+            tr = FastLocalityTrace(req, cfg.keys, topk=cfg.topk, reuse=cfg.reuse, zipf_s=cfg.zipf, seed=s)
+        else:
+            tr = LocalityTrace(req, cfg.keys, topk=cfg.topk, reuse=cfg.reuse, zipf_s=cfg.zipf, seed=s)
+        for i in range(n_steps):
+            out[i, layer] = tr.step()
+    return out
+
+
+def fold_layers(trace: np.ndarray, keys: int) -> np.ndarray:
+    """Layer l's ids become l * keys + id: one key space, one slot pool per request for all layers."""
+    off = (np.arange(trace.shape[1], dtype=np.int64) * keys)[None, :, None, None]
+    return (trace.astype(np.int64) + off).astype(np.int32)
+
+
 # ------------------------------------------------------------------ CPU side
 
-def make_trace(seed: int, n_steps: int) -> np.ndarray:
-    from asu_ascend_b200.workloads import LocalityTrace
+def cpu_port_run(cfg: ResolverCfg, req: int, trace: np.ndarray, prefill: int, timed: int, time_cap_s: float,
+                 threads: int):
+    """The C restatement of LRUManagedCache + the row copy on `threads` host cores.
 
-    tr = LocalityTrace(R, K, topk=Q, reuse=0.7, zipf_s=1.1, seed=seed)
-    return np.stack([tr.step() for _ in range(n_steps)])
-
-
-def cpu_port_run(trace: np.ndarray, prefill: int, timed: int, time_cap_s: float, threads: int):
-    """The C restatement of LRUManagedCache + the row copy on `threads` host cores."""
+    Returns (indices/s, layer-steps done, seconds).  The timed top-k sets are replayed in a
+    cycle until about time_cap_s of CPU work has been done.
+    """
     from asu_ascend_b200.workloads import record_addresses
     from oracle import c_oracle
 
+    kspace = cfg.keys * cfg.layers
     rng = np.random.Generator(np.random.PCG64(7))
-    host = rng.integers(0, 256, (POOL_ROWS, ROW), dtype=np.uint8)
-    rec = record_addresses(R, K, POOL_ROWS)
-    slot_pool = np.zeros((R, S, ROW), np.uint8)
-    pools = c_oracle.LruPools(R, K, S, TARGET)
+    rows = POOL_ROWS if cfg.row <= 4096 else POOL_ROWS // 64
+    host = rng.integers(0, 256, (rows, cfg.row), dtype=np.uint8)
+    rec = record_addresses(req, kspace, rows)
+    slot_pool = np.zeros((req, cfg.slots, cfg.row), np.uint8)
+    pools = c_oracle.LruPools(req, kspace, cfg.slots, cfg.target)
+    folded = fold_layers(trace, cfg.keys)
     for i in range(prefill):
-        pools.step_all(trace[i], threads=threads, want_outputs=False, host_pool=host, record=rec,
-                       slot_pool=slot_pool)
-    # The timed top-k sets are replayed in a cycle until about time_cap_s of CPU work has
-    # been done (one pass takes milliseconds on a many-core host).
+        for layer in range(cfg.layers):
+            pools.step_all(folded[i, layer], threads=threads, want_outputs=False, host_pool=host, record=rec,
+                           slot_pool=slot_pool)
     done, t_total = 0, 0.0
     while t_total < time_cap_s and done < 200000:
-        i = prefill + done % timed
+        i = prefill + (done // cfg.layers) % timed
+        layer = done % cfg.layers
         t0 = time.perf_counter()
-        pools.step_all(trace[i], threads=threads, want_outputs=True, host_pool=host, record=rec,
+        pools.step_all(folded[i, layer], threads=threads, want_outputs=True, host_pool=host, record=rec,
                        slot_pool=slot_pool)
         t_total += time.perf_counter() - t0
         done += 1
     pools.close()
-    return done * R * Q / t_total, done, t_total
+    return done * req * cfg.topk / t_total, done, t_total
 
 
 def run_reference(args, world: int, rank: int):
+    """Rank 0 times the CPU restatement on the default workload's config; other ranks exit."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    trace = make_trace(args.seed, args.prefill + args.warmup + args.steps)
-    value, done, secs = cpu_port_run(trace, args.prefill + args.warmup, args.steps, args.cpu_sample_s, threads)
-    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": done, "warmup": args.warmup,
-            "ms_per_step": secs / done * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int32", "data": "synthetic", "config": config_dict(1), "impl": "reference",
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"{done} steps x {R} requests x top-k {Q} ({secs:.1f} s, cycling the "
-                                       f"{args.steps} timed top-k sets after {args.prefill + args.warmup} untimed "
-                                       "steps), C restatement of LRUManagedCache + row memcpy, all host threads"},
-            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    cfg = RESOLVER_WORKLOADS["resolver"]
+    base = args.prefill + args.warmup
+    trace = make_trace(cfg, cfg.req, args.seed, base + args.steps)
+    value, done, secs = cpu_port_run(cfg, cfg.req, trace, base, args.steps, args.cpu_sample_s, threads)
+    line = base_line(world, done, args.warmup, secs / done * 1e3, value,
+                     {"workload": cfg.describe(), "requests_per_gpu": cfg.req, "topk": cfg.topk,
+                      "context": cfg.keys, "slots_per_request": cfg.slots, "row_bytes": cfg.row})
+    line.update({"impl": "reference",
+                 "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                                  "sample": f"{done} steps x {cfg.req} requests x top-k {cfg.topk} ({secs:.1f} s, "
+                                            f"cycling the {args.steps} timed top-k sets after {base} untimed steps), "
+                                            "C restatement of LRUManagedCache + row memcpy, all host threads"},
+                 "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
     print(json.dumps(line), flush=True)
 
 
-# ------------------------------------------------------------------ GPU side
+# ------------------------------------------------------------------ GPU helpers
 
 def h2d_peak_gbs(torch, dev) -> float:
     n = 256 << 20
@@ -201,100 +287,119 @@ def h2d_peak_gbs(torch, dev) -> float:
     return best
 
 
-def run_b200(args, world: int, rank: int, local_rank: int):
+class L2Flush:
+    """Write 256 MiB (evicts everything), then read another 256 MiB so the write-back of dirty lines
+    happens here, outside the timed region: the next step starts on a cold, clean L2."""
+
+    def __init__(self, torch, dev):
+        self.w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        self.r = torch.ones(64 << 20, dtype=torch.int32, device=dev)
+
+    def __call__(self):
+        self.w.zero_()
+        self.r.sum()
+
+
+# ------------------------------------------------------------------ resolver workloads
+
+def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int):
     import torch
-    import torch.distributed as dist
 
     import asu_ascend_b200
 
     asu_ascend_b200.load()
-    from asu_ascend_b200.dist import max_over_ranks, reduce_stats
+    from asu_ascend_b200.dist import max_over_ranks, reduce_stats, shard_range
     from asu_ascend_b200.host_pool import HostRowPool, check_status
     from asu_ascend_b200.lru import LruSlotPools
-    from asu_ascend_b200.workloads import record_addresses
+    from asu_ascend_b200.workloads import record_addresses_torch
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    K_steps, W = args.steps, args.warmup
-    n_steps = args.prefill + W + 2 * K_steps
-    trace = make_trace(args.seed + 1000 * rank, n_steps)
-    q_dev = torch.from_numpy(trace).to(dev)
-    q_host = torch.from_numpy(trace).pin_memory()
+    if cfg.strong:
+        r0, r1 = shard_range(cfg.req, world, rank)
+        R = r1 - r0
+    else:
+        r0, R = rank * cfg.req, cfg.req
+    K_steps, W, L = args.steps, args.warmup, cfg.layers
+    kspace = cfg.keys * L
+    base = args.prefill + W
+    n_steps = base + 2 * K_steps
+    trace = make_trace(cfg, R, args.seed + 1000 * (r0 + 1), n_steps)
+    folded = fold_layers(trace, cfg.keys)
+    q_dev = torch.from_numpy(folded).to(dev)
+    q_host = torch.from_numpy(folded).pin_memory()
 
-    host = HostRowPool(POOL_ROWS, ROW)
+    host = HostRowPool(POOL_ROWS if cfg.row <= 4096 else POOL_ROWS // 64, cfg.row)
     host.fill_random(11 + rank)
-    rec = torch.from_numpy(record_addresses(R, K, POOL_ROWS)).to(dev)
-    slot_pool = torch.zeros((R, S, ROW), dtype=torch.uint8, device=dev)
-    pools = LruSlotPools(R, K, S, TARGET, Q, device=dev)
+    rec = record_addresses_torch(R, kspace, host.rows, dev)
+    slot_pool = torch.zeros((R, cfg.slots, cfg.row), dtype=torch.uint8, device=dev)
+    pools = LruSlotPools(R, kspace, cfg.slots, cfg.target, cfg.topk, device=dev)
     outs = [pools.new_output(), pools.new_output()]
     status = torch.zeros(R, dtype=torch.int32, device=dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    flush_read = torch.ones(64 << 20, dtype=torch.int32, device=dev)  # 256 MiB
-
-    def flush_l2():
-        # Write 256 MiB (evicts everything), then read another 256 MiB so the write-back of the
-        # dirty lines happens here, outside the timed region: the step starts on a cold, clean L2.
-        flush.zero_()
-        flush_read.sum()
+    flush = L2Flush(torch, dev)
     h2d_peak = h2d_peak_gbs(torch, dev)
 
-    def step(i, o):
-        pools.step(q_dev[i], out=o)
-        host.swapin(rec, q_dev[i], o.slot, o.install, slot_pool, status=status)
-
-    for i in range(args.prefill + W):  # untimed: fill the pools, then warm up
-        step(i, outs[i % 2])
+    for i in range(base):  # untimed: fill the pools, then warm up
+        for layer in range(L):
+            o = outs[(i * L + layer) % 2]
+            pools.step(q_dev[i, layer], out=o)
+            host.swapin(rec, q_dev[i, layer], o.slot, o.install, slot_pool, status=status)
     torch.cuda.synchronize()
     if world > 1:
-        dist.barrier()
+        torch.distributed.barrier()
 
-    base = args.prefill + W
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K_steps)]
-    free_before = torch.empty(K_steps, dtype=torch.int64, device=dev)
-    free_after = torch.empty(K_steps, dtype=torch.int64, device=dev)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(1 + 2 * L)] for _ in range(K_steps)]
+    free_before = torch.empty(K_steps * L, dtype=torch.int64, device=dev)
+    free_after = torch.empty(K_steps * L, dtype=torch.int64, device=dev)
     stats0 = pools.stats.sum(0).clone()
-    gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[local_rank]) \
-        if os.environ.get("CUDA_VISIBLE_DEVICES") else local_rank
-    clocks = ClockSampler(gpu_index)
+    clocks = ClockSampler(gpu_index(local_rank))
     clocks.start()
     torch.cuda.synchronize()
     for k in range(K_steps):
-        o = outs[k % 2]
-        flush_l2()
-        free_before[k] = pools.free_count.sum()
+        flush()
         torch.cuda._sleep(100_000)  # keep the GPU busy while the host queues the step
         ev[k][0].record()
-        pools.step(q_dev[base + k], out=o)
-        ev[k][1].record()
-        host.swapin(rec, q_dev[base + k], o.slot, o.install, slot_pool, status=status)
-        ev[k][2].record()
-        free_after[k] = pools.free_count.sum()
+        for layer in range(L):
+            o = outs[(k * L + layer) % 2]
+            free_before[k * L + layer] = pools.free_count.sum()
+            q = q_dev[base + k, layer]
+            pools.step(q, out=o)
+            ev[k][1 + 2 * layer].record()
+            host.swapin(rec, q, o.slot, o.install, slot_pool, status=status)
+            ev[k][2 + 2 * layer].record()
+            free_after[k * L + layer] = pools.free_count.sum()
     torch.cuda.synchronize()
     clk = clocks.stop()
-    resolve_ms = [e[0].elapsed_time(e[1]) for e in ev]
-    swapin_ms = [e[1].elapsed_time(e[2]) for e in ev]
-    step_ms = [e[0].elapsed_time(e[2]) for e in ev]
+    resolve_ms, swapin_ms, step_ms = [], [], []
+    for e in ev:
+        prev = e[0]
+        for layer in range(L):
+            resolve_ms.append(prev.elapsed_time(e[1 + 2 * layer]))
+            swapin_ms.append(e[1 + 2 * layer].elapsed_time(e[2 + 2 * layer]))
+            prev = e[2 + 2 * layer]
+        step_ms.append(e[0].elapsed_time(e[-1]))
     d_stats = (pools.stats.sum(0) - stats0).cpu().tolist()
     installs, evictions = int(d_stats[2]), int(d_stats[4])
-    res0 = (R * S * K_steps - int(free_before.sum().item()))
-    res2 = (R * S * K_steps - int(free_after.sum().item()))
+    res0 = R * cfg.slots * K_steps * L - int(free_before.sum().item())
+    res2 = R * cfg.slots * K_steps * L - int(free_after.sum().item())
 
     # e2e through the public API: host top-k in, slot ids + hit mask out, copies timed
     base2 = base + K_steps
-    slot_host = torch.empty((R, Q), dtype=torch.int32, pin_memory=True)
-    hit_host = torch.empty((R, Q), dtype=torch.bool, pin_memory=True)
-    q_in = torch.empty((R, Q), dtype=torch.int32, device=dev)
+    slot_host = torch.empty((R, cfg.topk), dtype=torch.int32, pin_memory=True)
+    hit_host = torch.empty((R, cfg.topk), dtype=torch.bool, pin_memory=True)
+    q_in = torch.empty((R, cfg.topk), dtype=torch.int32, device=dev)
     ev2 = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K_steps)]
     for k in range(K_steps):
-        o = outs[k % 2]
-        flush_l2()
+        flush()
         torch.cuda._sleep(100_000)
         ev2[k][0].record()
-        q_in.copy_(q_host[base2 + k], non_blocking=True)
-        pools.step(q_in, out=o)
-        host.swapin(rec, q_in, o.slot, o.install, slot_pool, status=status)
-        slot_host.copy_(o.slot, non_blocking=True)
-        hit_host.copy_(o.hit, non_blocking=True)
+        for layer in range(L):
+            o = outs[(k * L + layer) % 2]
+            q_in.copy_(q_host[base2 + k, layer], non_blocking=True)
+            pools.step(q_in, out=o)
+            host.swapin(rec, q_in, o.slot, o.install, slot_pool, status=status)
+            slot_host.copy_(o.slot, non_blocking=True)
+            hit_host.copy_(o.hit, non_blocking=True)
         ev2[k][1].record()
     torch.cuda.synchronize()
     e2e_ms = [e[0].elapsed_time(e[1]) for e in ev2]
@@ -303,54 +408,194 @@ def run_b200(args, world: int, rank: int, local_rank: int):
 
     max_ms, max_e2e_ms = max_over_ranks([sum(step_ms), sum(e2e_ms)], dev)  # slowest rank
     job_stats = reduce_stats(pools.stats).cpu().tolist()  # end-of-run statistics (NCCL all-reduce)
+    job_req = cfg.req if cfg.strong else cfg.req * world
+    idx_per_step = job_req * cfg.topk * L
 
     if rank == 0:
         peaks = load_peaks()
         hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
-        alg_bytes = K_steps * R * Q * 14 + 4 * (res0 + res2) + 12 * installs + 20 * evictions
-        resolve_s = sum(resolve_ms) * 1e-3
-        achieved = alg_bytes / K_steps / (resolve_s / K_steps) / 1e9
-        swap_bytes = installs * ROW
-        swap_gbs = swap_bytes / (sum(swapin_ms) * 1e-3) / 1e9
+        launches = K_steps * L
+        alg_bytes = launches * R * cfg.topk * 14 + 4 * (res0 + res2) + 12 * installs + 20 * evictions
+        achieved = alg_bytes / (sum(resolve_ms) * 1e-3) / 1e9
+        swap_gbs = installs * cfg.row / (sum(swapin_ms) * 1e-3) / 1e9
         cpu = None
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and cfg.name == "resolver":
             threads = os.cpu_count() or 1
-            v, done, secs = cpu_port_run(trace, base, K_steps, args.cpu_sample_s, threads)
+            v, done, secs = cpu_port_run(cfg, R, trace, base, K_steps, args.cpu_sample_s, threads)
             cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                   "sample": f"{done} steps x {R} requests x top-k {Q} ({secs:.1f} s, cycling the {K_steps} timed "
-                             "top-k sets of this workload), C restatement of LRUManagedCache + row memcpy, all host "
-                             "threads"}
-        line = {
-            "metric": METRIC, "value": world * R * Q * K_steps / (max_ms * 1e-3), "unit": UNIT, "n_gpus": world,
-            "steps": K_steps, "warmup": W, "ms_per_step": max_ms / K_steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int32", "data": "synthetic",
-            "config": config_dict(world),
+                   "sample": f"{done} steps x {R} requests x top-k {cfg.topk} ({secs:.1f} s, cycling the "
+                             f"{K_steps} timed top-k sets of this workload), C restatement of LRUManagedCache + "
+                             "row memcpy, all host threads"}
+        config = {"workload": cfg.describe(), "requests_per_gpu": R, "global_batch": job_req, "topk": cfg.topk,
+                  "layers": L, "context": cfg.keys, "slots_per_request": cfg.slots, "free_target": cfg.target,
+                  "row_bytes": cfg.row,
+                  "locality": (f"{int(cfg.reuse * 100)}% reuse + "
+                               + (f"zipf({cfg.zipf})" if cfg.zipf else "uniform")),
+                  "l2": L2_NOTE, "parallelism": f"request-sharded x{world}", "prefill_steps": args.prefill}
+        line = base_line(world, K_steps, W, max_ms / K_steps, idx_per_step * K_steps / (max_ms * 1e-3), config,
+                         scaling="strong" if cfg.strong else "weak")
+        line.update({
             "p50_resolve_us": statistics.median(resolve_ms) * 1e3,
             "p50_swapin_us": statistics.median(swapin_ms) * 1e3,
-            "miss_rate": installs / (K_steps * R * Q),
+            "miss_rate": installs / (launches * R * cfg.topk),
             "swapin_gbs": swap_gbs,
-            # dominant kernel by time (ncu launch list: ~93% of the step) -- bound by the host link
+            # dominant kernel by time (ncu launch list: ~93% of the resolver step), bound by the host link
             "roofline": {"bound": "host_link", "kernel": "swapin_kernel", "achieved": swap_gbs, "peak": h2d_peak,
                          "unit": "GB/s", "frac": swap_gbs / h2d_peak,
-                         "traffic": SWAPIN_PCIE_READ_BYTES_PER_LAUNCH * installs / K_steps / SWAPIN_NCU_INSTALLS,
-                         "traffic_kind": "PCIe read bytes per launch (ncu pcie__read_bytes, scaled to this run's "
-                                         "installs per step)",
+                         "traffic": (SWAPIN_PCIE_READ_BYTES_PER_LAUNCH * installs / launches / SWAPIN_NCU_INSTALLS
+                                     if cfg.row == 656 else None),
+                         "traffic_kind": "PCIe read bytes per launch (ncu pcie__read_bytes of the resolver "
+                                         "workload, scaled to this run's installs per launch)",
                          "peak_source": "pinned cudaMemcpyAsync H2D 256 MiB, best of 10, this run"},
             "roofline_lru": {"bound": "hbm", "kernel": "lru_step_kernel", "achieved": achieved, "peak": hbm_peak,
                              "unit": "GB/s", "frac": achieved / hbm_peak,
-                             "traffic": LRU_DRAM_BYTES_PER_LAUNCH,
+                             "traffic": LRU_DRAM_BYTES_PER_LAUNCH if cfg.name == "resolver" else None,
                              "traffic_kind": "dram__bytes_read.sum + dram__bytes_write.sum of one launch (ncu)",
-                             "algorithmic_bytes_per_launch": alg_bytes / K_steps,
+                             "algorithmic_bytes_per_launch": alg_bytes / launches,
                              "peak_source": "measured HBM copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"},
-            "e2e": {"value": world * R * Q * K_steps / (max_e2e_ms * 1e-3), "unit": UNIT,
-                    "h2d_bytes_per_step": R * Q * 4, "d2h_bytes_per_step": R * Q * 5},
-            "gpu_launches": 2 * K_steps,
+            "e2e": {"value": idx_per_step * K_steps / (max_e2e_ms * 1e-3), "unit": UNIT,
+                    "h2d_bytes_per_step": R * cfg.topk * 4 * L, "d2h_bytes_per_step": R * cfg.topk * 5 * L},
+            "gpu_launches": 2 * launches,
             "job_stats": dict(zip(LruSlotPools.STAT_NAMES, job_stats)),
             "cpu_baseline": cpu,
             "clocks": clk,
-        }
+        })
         print(json.dumps(line), flush=True)
     host.close()
+
+
+# ------------------------------------------------------------------ single-request LRU (CPU reference config)
+
+def run_lru1(args, world: int, rank: int, local_rank: int):
+    import torch
+
+    import asu_ascend_b200
+
+    asu_ascend_b200.load()
+    from asu_ascend_b200.dist import max_over_ranks
+    from asu_ascend_b200.lru import LruSlotPools
+    from asu_ascend_b200.workloads import LocalityTrace
+    from oracle import c_oracle
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    n = args.prefill + args.warmup + args.steps
+    tr = LocalityTrace(1, 131072, topk=2048, reuse=0.7, zipf_s=1.1, seed=0)  # the reference-pinned c0 trace
+    trace = np.stack([tr.step() for _ in range(n)])
+    q = torch.from_numpy(trace).to(dev)
+    pools = LruSlotPools(1, 131072, 16384, 2048, 2048, device=dev)
+    flush = L2Flush(torch, dev)
+    base = args.prefill + args.warmup
+    for i in range(base):
+        pools.step(q[i])
+    ms = []
+    for k in range(args.steps):
+        flush()
+        torch.cuda._sleep(100_000)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        pools.step(q[base + k])
+        b.record()
+        b.synchronize()
+        ms.append(a.elapsed_time(b))
+    pools.check_status()
+    (tot_ms,) = max_over_ranks([sum(ms)], dev)
+    cpu = c_oracle.LruPools(1, 131072, 16384, 2048)
+    for i in range(base):
+        cpu.step_all(trace[i], threads=1, want_outputs=False)
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        cpu.step_all(trace[base + k], threads=1)
+    cpu_s = time.perf_counter() - t0
+    cpu.close()
+    if rank == 0:
+        line = base_line(world, args.steps, args.warmup, tot_ms / args.steps,
+                         world * 2048 * args.steps / (tot_ms * 1e-3),
+                         {"workload": "lru1: 1 request/GPU, 131072 keys, 16384 slots, LRU target 2048, top-k 2048 "
+                                      "(70% reuse + zipf 1.1), maintain + lookup only", "l2": L2_NOTE})
+        line.update({"p50_resolve_us": statistics.median(ms) * 1e3, "gpu_launches": args.steps,
+                     "cpu_baseline": {"value": 2048 * args.steps / cpu_s, "unit": UNIT, "cores": 1, "kind": "port",
+                                      "sample": f"the same {args.steps} steps, C restatement, one thread"},
+                     "e2e": None})
+        print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ pure lookup
+
+def run_lookup(args, world: int, rank: int, local_rank: int):
+    import torch
+
+    import asu_ascend_b200
+
+    asu_ascend_b200.load()
+    from asu_ascend_b200 import hbm_lookup_update as H
+    from asu_ascend_b200.dist import max_over_ranks
+    from asu_ascend_b200.workloads import lookup_only_case
+    from oracle import asu_oracle as O
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    table, query = lookup_only_case(seed=1 + rank)
+    tt, tq = torch.from_numpy(table).to(dev), torch.from_numpy(query).to(dev)
+    out = torch.empty_like(tq)
+    hit = torch.empty(tq.shape, dtype=torch.bool, device=dev)
+    flush = L2Flush(torch, dev)
+    for _ in range(args.warmup):
+        H.lookup(tt, tq, out=out, hit=hit)
+    ms, ms_e2e = [], []
+    q_host = torch.from_numpy(query).pin_memory()
+    out_host = torch.empty(query.shape, dtype=torch.int32, pin_memory=True)
+    hit_host = torch.empty(query.shape, dtype=torch.bool, pin_memory=True)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for k in range(args.steps):
+        flush()
+        torch.cuda._sleep(100_000)
+        a.record()
+        H.lookup(tt, tq, out=out, hit=hit)
+        b.record()
+        b.synchronize()
+        ms.append(a.elapsed_time(b))
+        flush()
+        torch.cuda._sleep(100_000)
+        a.record()
+        tq.copy_(q_host, non_blocking=True)
+        H.lookup(tt, tq, out=out, hit=hit)
+        out_host.copy_(out, non_blocking=True)
+        hit_host.copy_(hit, non_blocking=True)
+        b.record()
+        b.synchronize()
+        ms_e2e.append(a.elapsed_time(b))
+    exp, _ = O.gather_lookup(table, query)
+    if not (out.cpu().numpy() == exp).all():
+        raise RuntimeError("lookup output differs from the oracle")
+    tot_ms, tot_e2e = max_over_ranks([sum(ms), sum(ms_e2e)], dev)
+    if rank == 0:
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < 3.0:
+            O.gather_lookup(table, query)
+            reps += 1
+        cpu_s = (time.perf_counter() - t0) / reps
+        n = query.size
+        value = world * n * args.steps / (tot_ms * 1e-3)
+        line = base_line(world, args.steps, args.warmup, tot_ms / args.steps, value,
+                         {"workload": "lookup: 64 req/GPU x 2048 queries, 64 x 128K int32 tables with 4096 "
+                                      "resident entries, ~85% hits, slot ids + hit mask", "l2": L2_NOTE},
+                         vs=value / world / REF_LOOKUP_IDX_PER_S)
+        hbm = float(load_peaks().get("hbm_gbs", 6650.0))
+        achieved = n * 13 / (statistics.median(ms) * 1e-3) / 1e9
+        line.update({"p50_lookup_us": statistics.median(ms) * 1e3,
+                     "vs_baseline_note": "per GPU vs 2.93e8 indices/s implied by 50x2048 lookups in 350 us on "
+                                         "Ascend 910B (docs/archive/hbm_kvcache_lookup_recommendations.md:32)",
+                     "roofline": {"bound": "hbm", "kernel": "gather_vec4_kernel", "achieved": achieved, "peak": hbm,
+                                  "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                                  "algorithmic_bytes_per_launch": n * 13},
+                     "e2e": {"value": world * n * args.steps / (tot_e2e * 1e-3), "unit": UNIT,
+                             "h2d_bytes_per_step": n * 4, "d2h_bytes_per_step": n * 5},
+                     "gpu_launches": args.steps,
+                     "cpu_baseline": {"value": n / cpu_s, "unit": UNIT, "cores": 1, "kind": "port",
+                                      "sample": "numpy restatement of the reference gather, same 64 x 2048 batch"}})
+        print(json.dumps(line), flush=True)
 
 
 def main():
@@ -368,7 +613,12 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
     try:
-        run_b200(args, world, rank, local_rank)
+        if args.workload in RESOLVER_WORKLOADS:
+            run_resolver(args, RESOLVER_WORKLOADS[args.workload], world, rank, local_rank)
+        elif args.workload == "lru1":
+            run_lru1(args, world, rank, local_rank)
+        else:
+            run_lookup(args, world, rank, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist
