@@ -150,14 +150,20 @@ def record_addresses(req_num: int, key_space: int, pool_rows: int) -> np.ndarray
     return (((r * key_space + k) * RECORD_SALT + RECORD_OFFSET) % pool_rows).astype(np.int32)
 
 
-def record_addresses_torch(req_num: int, key_space: int, pool_rows: int, device):
-    """record_addresses computed on ``device`` (same values), for tables too large for host RAM."""
+def record_addresses_torch(req_num: int, key_space: int, pool_rows: int, device, key_offset: int = 0,
+                           row_stride: int | None = None):
+    """record_addresses computed on ``device`` (same values), for tables too large for host RAM.
+
+    ``key_offset`` / ``row_stride`` select the columns [key_offset, key_offset + key_space) of a
+    wider table with ``row_stride`` keys per request (one layer of a multi-layer record space).
+    """
     import torch
 
+    stride = key_space if row_stride is None else row_stride
     out = torch.empty((req_num, key_space), dtype=torch.int32, device=device)
-    k = torch.arange(key_space, dtype=torch.int64, device=device)
+    k = torch.arange(key_space, dtype=torch.int64, device=device) + key_offset
     for r in range(req_num):
-        out[r] = ((r * key_space + k) * RECORD_SALT + RECORD_OFFSET).remainder(pool_rows).to(torch.int32)
+        out[r] = ((r * stride + k) * RECORD_SALT + RECORD_OFFSET).remainder(pool_rows).to(torch.int32)
     return out
 
 

@@ -18,7 +18,7 @@ Other workloads (`--workload`):
   lru1          1 request, 128K keys, 16384 slots, target 2048, LRU maintain + lookup only
   lookup        64 x 2048 queries gathered from 64 x 128K tables (4096 resident), hit mask
   multilayer    1024 requests split over the GPUs (strong scaling), 4 layers per decode
-                step with independent top-k, one 8192-slot pool per request shared by them
+                step with independent top-k, an 8192-slot pool per request and layer
   stress        128 requests, 1M-token context, top-k 2048, 20% reuse + uniform draws
   stress-block  the stress context in 64-token blocks: top-k 32 blocks, 128 block slots,
                 41,984-byte rows
@@ -85,6 +85,8 @@ class ResolverCfg:
 
 RESOLVER_WORKLOADS = {
     "resolver": ResolverCfg("resolver", 128, 131072, 8192, 2048, 2048, 656),
+    # 4 layers, each with its own 8192-slot pool per request (one LRU pool shared by 4 x 2048
+    # keys per step would cycle through more keys than it holds and never hit)
     "multilayer": ResolverCfg("multilayer", 1024, 131072, 8192, 2048, 2048, 656, layers=4, strong=True,
                               fast_trace=True),
     "stress": ResolverCfg("stress", 128, 1 << 20, 8192, 2048, 2048, 656, reuse=0.2, zipf=None, fast_trace=True),
@@ -321,64 +323,65 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     else:
         r0, R = rank * cfg.req, cfg.req
     K_steps, W, L = args.steps, args.warmup, cfg.layers
-    kspace = cfg.keys * L
     base = args.prefill + W
     n_steps = base + 2 * K_steps
     trace = make_trace(cfg, R, args.seed + 1000 * (r0 + 1), n_steps)
-    folded = fold_layers(trace, cfg.keys)
-    q_dev = torch.from_numpy(folded).to(dev)
-    q_host = torch.from_numpy(folded).pin_memory()
+    q_dev = torch.from_numpy(trace).to(dev)
+    q_host = torch.from_numpy(trace).pin_memory()
 
+    # One pool per (layer, request), as the reference manager keeps one managed cache per layer
+    # (patch/0003 asu_kv_cache_manager.py from_kv_caches, patch lines 339-403).
     host = HostRowPool(POOL_ROWS if cfg.row <= 4096 else POOL_ROWS // 64, cfg.row)
     host.fill_random(11 + rank)
-    rec = record_addresses_torch(R, kspace, host.rows, dev)
-    slot_pool = torch.zeros((R, cfg.slots, cfg.row), dtype=torch.uint8, device=dev)
-    pools = LruSlotPools(R, kspace, cfg.slots, cfg.target, cfg.topk, device=dev)
-    outs = [pools.new_output(), pools.new_output()]
+    recs = [record_addresses_torch(R, cfg.keys, host.rows, dev, key_offset=layer * cfg.keys,
+                                   row_stride=cfg.keys * L) for layer in range(L)]
+    slot_pools = [torch.zeros((R, cfg.slots, cfg.row), dtype=torch.uint8, device=dev) for _ in range(L)]
+    pools = [LruSlotPools(R, cfg.keys, cfg.slots, cfg.target, cfg.topk, device=dev) for _ in range(L)]
+    outs = [pools[0].new_output(), pools[0].new_output()]
     status = torch.zeros(R, dtype=torch.int32, device=dev)
     flush = L2Flush(torch, dev)
     h2d_peak = h2d_peak_gbs(torch, dev)
 
+    def total_stats():
+        return sum(p.stats.sum(0) for p in pools)
+
     for i in range(base):  # untimed: fill the pools, then warm up
         for layer in range(L):
             o = outs[(i * L + layer) % 2]
-            pools.step(q_dev[i, layer], out=o)
-            host.swapin(rec, q_dev[i, layer], o.slot, o.install, slot_pool, status=status)
+            pools[layer].step(q_dev[i, layer], out=o)
+            host.swapin(recs[layer], q_dev[i, layer], o.slot, o.install, slot_pools[layer], status=status)
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
 
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(1 + 2 * L)] for _ in range(K_steps)]
+    # per step and layer: [a] resolve [b] swap-in [c]; the free-count snapshots sit outside
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(L)] for _ in range(K_steps)]
     free_before = torch.empty(K_steps * L, dtype=torch.int64, device=dev)
     free_after = torch.empty(K_steps * L, dtype=torch.int64, device=dev)
-    stats0 = pools.stats.sum(0).clone()
+    stats0 = total_stats().clone()
     clocks = ClockSampler(gpu_index(local_rank))
     clocks.start()
     torch.cuda.synchronize()
     for k in range(K_steps):
         flush()
         torch.cuda._sleep(100_000)  # keep the GPU busy while the host queues the step
-        ev[k][0].record()
         for layer in range(L):
             o = outs[(k * L + layer) % 2]
-            free_before[k * L + layer] = pools.free_count.sum()
+            free_before[k * L + layer] = pools[layer].free_count.sum()
             q = q_dev[base + k, layer]
-            pools.step(q, out=o)
-            ev[k][1 + 2 * layer].record()
-            host.swapin(rec, q, o.slot, o.install, slot_pool, status=status)
-            ev[k][2 + 2 * layer].record()
-            free_after[k * L + layer] = pools.free_count.sum()
+            a, b, c = ev[k][layer]
+            a.record()
+            pools[layer].step(q, out=o)
+            b.record()
+            host.swapin(recs[layer], q, o.slot, o.install, slot_pools[layer], status=status)
+            c.record()
+            free_after[k * L + layer] = pools[layer].free_count.sum()
     torch.cuda.synchronize()
     clk = clocks.stop()
-    resolve_ms, swapin_ms, step_ms = [], [], []
-    for e in ev:
-        prev = e[0]
-        for layer in range(L):
-            resolve_ms.append(prev.elapsed_time(e[1 + 2 * layer]))
-            swapin_ms.append(e[1 + 2 * layer].elapsed_time(e[2 + 2 * layer]))
-            prev = e[2 + 2 * layer]
-        step_ms.append(e[0].elapsed_time(e[-1]))
-    d_stats = (pools.stats.sum(0) - stats0).cpu().tolist()
+    resolve_ms = [a.elapsed_time(b) for step in ev for a, b, _ in step]
+    swapin_ms = [b.elapsed_time(c) for step in ev for _, b, c in step]
+    step_ms = [sum(a.elapsed_time(c) for a, _, c in step) for step in ev]
+    d_stats = (total_stats() - stats0).cpu().tolist()
     installs, evictions = int(d_stats[2]), int(d_stats[4])
     res0 = R * cfg.slots * K_steps * L - int(free_before.sum().item())
     res2 = R * cfg.slots * K_steps * L - int(free_after.sum().item())
@@ -396,18 +399,19 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
         for layer in range(L):
             o = outs[(k * L + layer) % 2]
             q_in.copy_(q_host[base2 + k, layer], non_blocking=True)
-            pools.step(q_in, out=o)
-            host.swapin(rec, q_in, o.slot, o.install, slot_pool, status=status)
+            pools[layer].step(q_in, out=o)
+            host.swapin(recs[layer], q_in, o.slot, o.install, slot_pools[layer], status=status)
             slot_host.copy_(o.slot, non_blocking=True)
             hit_host.copy_(o.hit, non_blocking=True)
         ev2[k][1].record()
     torch.cuda.synchronize()
     e2e_ms = [e[0].elapsed_time(e[1]) for e in ev2]
-    pools.check_status()
+    for p in pools:
+        p.check_status()
     check_status(status, "swapin")
 
     max_ms, max_e2e_ms = max_over_ranks([sum(step_ms), sum(e2e_ms)], dev)  # slowest rank
-    job_stats = reduce_stats(pools.stats).cpu().tolist()  # end-of-run statistics (NCCL all-reduce)
+    job_stats = reduce_stats(torch.stack([p.stats for p in pools])).cpu().tolist()  # end-of-run (NCCL)
     job_req = cfg.req if cfg.strong else cfg.req * world
     idx_per_step = job_req * cfg.topk * L
 
@@ -457,6 +461,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
                     "h2d_bytes_per_step": R * cfg.topk * 4 * L, "d2h_bytes_per_step": R * cfg.topk * 5 * L},
             "gpu_launches": 2 * launches,
             "job_stats": dict(zip(LruSlotPools.STAT_NAMES, job_stats)),
+            "note_step_time": "sum over layers of (resolve + swap-in) event intervals",
             "cpu_baseline": cpu,
             "clocks": clk,
         })
