@@ -55,7 +55,8 @@ _SIGS = {
     "asu_hbm_index_lookup_simt_ex": [_P, _P, _P, _P, _P, _P, _P, c_uint32, c_uint32, c_uint32, c_uint32, _P],
     "asu_lru_step": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, c_uint32, _P, _P, _P, c_uint32, c_uint32, c_uint32,
                      c_uint32, c_uint32],
-    "asu_swapin_gather": [_P, _P, c_int64, c_uint32, _P, c_uint32, _P, _P, _P, c_uint32, _P, c_uint32, c_uint32, _P],
+    "asu_swapin_gather": [_P, _P, c_int64, c_uint32, c_uint32, _P, c_uint32, _P, _P, _P, c_uint32, _P, c_uint32,
+                          c_uint32, _P],
     "asu_host_pool_alloc": [c_uint64, POINTER(c_void_p), POINTER(c_void_p)],
     "asu_host_pool_free": [_P],
     "asu_kv_resolver_do": [_P, _P, c_int64, _P, _P, _P, _P, _P, _P, c_int64, _P, c_int64, _P, _P, _P, _P, c_int64,

@@ -6,7 +6,8 @@
 // (docs/v0.1/kv-cache-offload-v0.1-real-ops-design.md:293-312; MicroKV/src/server.cpp:220-251).
 // The bytes that land in slot `s` are the record's bytes, unchanged.
 //
-// B200 design: zero-copy.  The host pool is page-locked and mapped, so the GPU reads it
+// B200 design: zero-copy.  The host pool is page-locked and mapped (rows host_pitch bytes
+// apart, 128-byte aligned by default), so the GPU reads it
 // directly over the host link with 16-byte loads and writes 16-byte stores into HBM; no
 // host thread, no staging copy, no synchronisation with the CPU.  Work unit: one warp per
 // 32 query positions of one request.  The warp ballots the install flags, compacts the
@@ -23,8 +24,9 @@ constexpr int kWarps = 8;
 constexpr int kUnroll = 8;
 
 __global__ void __launch_bounds__(kWarps * 32)
-swapin_kernel(const int4* host, int64_t pool_rows, uint32_t cpr, const int32_t* __restrict__ rec, uint32_t K,
-              const int32_t* __restrict__ query, const int32_t* __restrict__ slot,
+swapin_kernel(const int4* host, int64_t pool_rows, uint32_t cpr, uint32_t pitch16,
+              const int32_t* __restrict__ rec, uint32_t K, const int32_t* __restrict__ query,
+              const int32_t* __restrict__ slot,
               const uint8_t* __restrict__ inst, uint32_t Q, int4* __restrict__ pool, uint32_t S, uint32_t R,
               int32_t* status) {
     __shared__ int64_t src_row[kWarps][32];
@@ -79,7 +81,7 @@ swapin_kernel(const int4* host, int64_t pool_rows, uint32_t cpr, const int32_t* 
                 if (c < total) {
                     const uint32_t ri = c / cpr;
                     const uint32_t ch = c - ri * cpr;
-                    buf[u] = host[src_row[w][ri] * cpr + ch];
+                    buf[u] = host[src_row[w][ri] * pitch16 + ch];
                 }
             }
 #pragma unroll
@@ -102,22 +104,25 @@ swapin_kernel(const int4* host, int64_t pool_rows, uint32_t cpr, const int32_t* 
 using namespace asu;
 
 extern "C" int asu_swapin_gather(void* stream, const void* host_pool, int64_t pool_rows, uint32_t row_bytes,
-                                 const int32_t* record_addr, uint32_t key_space, const int32_t* query,
-                                 const int32_t* slot, const uint8_t* install_mask, uint32_t query_count,
+                                 uint32_t host_pitch, const int32_t* record_addr, uint32_t key_space,
+                                 const int32_t* query, const int32_t* slot, const uint8_t* install_mask,
+                                 uint32_t query_count,
                                  void* slot_pool, uint32_t slot_count, uint32_t req_num, int32_t* status) {
     if (req_num == 0 || query_count == 0) return ASU_OK;
     if (!host_pool || !record_addr || !query || !slot || !install_mask || !slot_pool || pool_rows <= 0 ||
         row_bytes == 0 || key_space == 0 || slot_count == 0)
         return ASU_ERR_ARG;
-    if (row_bytes % 16 != 0 || reinterpret_cast<uintptr_t>(host_pool) % 16 != 0 ||
+    if (host_pitch == 0) host_pitch = row_bytes;
+    if (host_pitch < row_bytes) return ASU_ERR_ARG;
+    if (row_bytes % 16 != 0 || host_pitch % 16 != 0 || reinterpret_cast<uintptr_t>(host_pool) % 16 != 0 ||
         reinterpret_cast<uintptr_t>(slot_pool) % 16 != 0)
         return ASU_ERR_ALIGN;
     const uint64_t groups = static_cast<uint64_t>(req_num) * ((query_count + 31) / 32);
     uint64_t grid = (groups + kWarps - 1) / kWarps;
     if (grid > 148ull * 8ull) grid = 148ull * 8ull;
     swapin_kernel<<<static_cast<uint32_t>(grid), kWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const int4*>(host_pool), pool_rows, row_bytes / 16, record_addr, key_space, query, slot,
-        install_mask, query_count, static_cast<int4*>(slot_pool), slot_count, req_num, status);
+        static_cast<const int4*>(host_pool), pool_rows, row_bytes / 16, host_pitch / 16, record_addr, key_space,
+        query, slot, install_mask, query_count, static_cast<int4*>(slot_pool), slot_count, req_num, status);
     return asu_launch_status();
 }
 

@@ -19,18 +19,28 @@ from ._lib import check, lib, raise_on_status
 
 
 class HostRowPool:
-    def __init__(self, rows: int, row_bytes: int):
+    """``rows`` records of ``row_bytes`` bytes in page-locked, GPU-mapped host memory.
+
+    Consecutive rows start ``pitch`` bytes apart (default: row_bytes rounded up to 128, so a
+    656-byte DSA row occupies whole 128-byte host-link reads).  ``array`` is a [rows, row_bytes]
+    view of the records.
+    """
+
+    def __init__(self, rows: int, row_bytes: int, pitch: int | None = None):
         if rows <= 0 or row_bytes <= 0 or row_bytes % 16:
             raise ValueError("rows must be positive and row_bytes a positive multiple of 16")
-        self.rows, self.row_bytes = rows, row_bytes
-        self.nbytes = rows * row_bytes
+        pitch = (row_bytes + 127) // 128 * 128 if pitch is None else pitch
+        if pitch < row_bytes or pitch % 16:
+            raise ValueError("pitch must be a multiple of 16 and at least row_bytes")
+        self.rows, self.row_bytes, self.pitch = rows, row_bytes, pitch
+        self.nbytes = rows * pitch
         host = ctypes.c_void_p()
         dev = ctypes.c_void_p()
         check(lib.asu_host_pool_alloc(self.nbytes, ctypes.byref(host), ctypes.byref(dev)), "asu_host_pool_alloc")
         self._host = host.value
         self.device_ptr = dev.value
         buf = (ctypes.c_uint8 * self.nbytes).from_address(self._host)
-        self.array = np.frombuffer(buf, dtype=np.uint8).reshape(rows, row_bytes)
+        self.array = np.frombuffer(buf, dtype=np.uint8).reshape(rows, pitch)[:, :row_bytes]
         self.tensor = torch.from_numpy(self.array)  # CPU view of the same pinned bytes
 
     def fill_random(self, seed: int) -> None:
@@ -74,7 +84,7 @@ class HostRowPool:
         s = (stream or torch.cuda.current_stream(dev)).cuda_stream
         with torch.cuda.device(dev):
             check(lib.asu_swapin_gather(
-                s, self.device_ptr, self.rows, self.row_bytes, record_addr.data_ptr(), record_addr.shape[1],
+                s, self.device_ptr, self.rows, self.row_bytes, self.pitch, record_addr.data_ptr(), record_addr.shape[1],
                 query.data_ptr(), slot.data_ptr(), install.data_ptr(), Q, slot_pool.data_ptr(), slot_pool.shape[1],
                 R, None if status is None else status.data_ptr()), "asu_swapin_gather")
 

@@ -107,6 +107,8 @@ def parse_args():
     p.add_argument("--seed", type=int, default=2026)
     p.add_argument("--cpu-sample-s", type=float, default=12.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--host-pitch", type=int, default=0,
+                   help="bytes between host-pool rows (0: row size rounded up to 128)")
     return p.parse_args()
 
 
@@ -331,7 +333,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
 
     # One pool per (layer, request), as the reference manager keeps one managed cache per layer
     # (patch/0003 asu_kv_cache_manager.py from_kv_caches, patch lines 339-403).
-    host = HostRowPool(POOL_ROWS if cfg.row <= 4096 else POOL_ROWS // 64, cfg.row)
+    host = HostRowPool(POOL_ROWS if cfg.row <= 4096 else POOL_ROWS // 64, cfg.row, pitch=args.host_pitch or None)
     host.fill_random(11 + rank)
     recs = [record_addresses_torch(R, cfg.keys, host.rows, dev, key_offset=layer * cfg.keys,
                                    row_stride=cfg.keys * L) for layer in range(L)]
@@ -435,7 +437,8 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
                   "row_bytes": cfg.row,
                   "locality": (f"{int(cfg.reuse * 100)}% reuse + "
                                + (f"zipf({cfg.zipf})" if cfg.zipf else "uniform")),
-                  "l2": L2_NOTE, "parallelism": f"request-sharded x{world}", "prefill_steps": args.prefill}
+                  "host_pitch": host.pitch, "l2": L2_NOTE, "parallelism": f"request-sharded x{world}",
+                  "prefill_steps": args.prefill}
         line = base_line(world, K_steps, W, max_ms / K_steps, idx_per_step * K_steps / (max_ms * 1e-3), config,
                          scaling="strong" if cfg.strong else "weak")
         line.update({

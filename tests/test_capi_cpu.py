@@ -62,8 +62,10 @@ def test_argument_validation_rejects_before_launch(lib):
     assert L.asu_lru_step(None, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 4, 1, None, None, 1, 100, 64, 16, 8) == \
         lib.ASU_ERR_ARG  # evicted row narrower than the free target
     # swap-in alignment
-    assert L.asu_swapin_gather(None, 16, 10, 24, 1, 1, 1, 1, 1, 4, 16, 4, 1, None) == lib.ASU_ERR_ALIGN
-    assert L.asu_swapin_gather(None, 8, 10, 32, 1, 1, 1, 1, 1, 4, 16, 4, 1, None) == lib.ASU_ERR_ALIGN
+    assert L.asu_swapin_gather(None, 16, 10, 24, 0, 1, 1, 1, 1, 1, 4, 16, 4, 1, None) == lib.ASU_ERR_ALIGN
+    assert L.asu_swapin_gather(None, 8, 10, 32, 0, 1, 1, 1, 1, 1, 4, 16, 4, 1, None) == lib.ASU_ERR_ALIGN
+    assert L.asu_swapin_gather(None, 16, 10, 32, 40, 1, 1, 1, 1, 1, 4, 16, 4, 1, None) == lib.ASU_ERR_ALIGN
+    assert L.asu_swapin_gather(None, 16, 10, 32, 16, 1, 1, 1, 1, 1, 4, 16, 4, 1, None) == lib.ASU_ERR_ARG
     # resolver: block_size 0
     assert L.asu_kv_resolver_do(None, 1, 4, 1, 1, 1, 1, 1, 1, 4, 1, 1, 1, 1, 1, 1, 4, 4, 4, 4, 4, 4, 0, 1, 1,
                                 None) == lib.ASU_ERR_ARG
