@@ -7,7 +7,7 @@
 // The bytes that land in slot `s` are the record's bytes, unchanged.
 //
 // B200 design: zero-copy.  The host pool is page-locked and mapped (rows host_pitch bytes
-// apart, 128-byte aligned by default), so the GPU reads it
+// apart), so the GPU reads it
 // directly over the host link with 16-byte loads and writes 16-byte stores into HBM; no
 // host thread, no staging copy, no synchronisation with the CPU.  Work unit: one warp per
 // 32 query positions of one request.  The warp ballots the install flags, compacts the

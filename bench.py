@@ -108,7 +108,7 @@ def parse_args():
     p.add_argument("--cpu-sample-s", type=float, default=12.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--host-pitch", type=int, default=0,
-                   help="bytes between host-pool rows (0: row size rounded up to 128)")
+                   help="bytes between host-pool rows (0: packed rows)")
     return p.parse_args()
 
 

@@ -180,8 +180,7 @@ int asu_lru_step(void* stream, int32_t* token_to_slot, int32_t* slot_to_token, i
  * row_bytes; device-accessible mapped pinned memory) into slot_pool[r, slot[r,pos]]
  * ([req, slot_count, row_bytes], HBM).  Replaces the MicroKV batch_get + H2D of the v0.1 design
  * (docs/v0.1/kv-cache-offload-v0.1-real-ops-design.md:293-312).  row_bytes and host_pitch must
- * be multiples of 16 and both pools 16-byte aligned; a 128-byte pitch keeps every row on whole
- * 128-byte host-link reads. */
+ * be multiples of 16 and both pools 16-byte aligned. */
 int asu_swapin_gather(void* stream, const void* host_pool, int64_t pool_rows, uint32_t row_bytes,
                       uint32_t host_pitch, const int32_t* record_addr, uint32_t key_space, const int32_t* query,
                       const int32_t* slot,
