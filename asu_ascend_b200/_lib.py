@@ -62,6 +62,7 @@ _SIGS = {
     "asu_kv_resolver_do": [_P, _P, c_int64, _P, _P, _P, _P, _P, _P, c_int64, _P, c_int64, _P, _P, _P, _P, c_int64,
                            c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, _P, _P, _P],
     "asu_kv_resolver_workspace_bytes": [c_int64],
+    "asu_resolver_reset": [_P, _P, _P, _P, c_int64, _P, _P, _P, c_int64, _P, c_int64, c_int64, c_int64, c_int64],
     "asu_kv_resolver_noalloc": [_P, _P, c_int64, _P, _P, _P, _P, _P, _P, c_int64, _P, c_int64, _P, _P, _P, _P,
                                 c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, _P, _P],
 }

@@ -198,15 +198,19 @@ def npu_asu_resolve_kv_slots_single_req(original_topk_indices, actual_seq_len, m
     slot_count = min(m0.shape[0], m1.shape[0], slot_owner_token.numel())
     max_seq = min(token_state.numel(), hbm_slot_of_token.numel(), record.numel())
     ws = torch.empty(int(lib.asu_kv_resolver_workspace_bytes(n)), dtype=torch.uint8, device=dev)
-    status = _new_status(1, dev)
+    # the status word is only read when status checks are on; without them the kernel gets no
+    # status pointer and the call launches exactly the resolver's two kernels
+    status = _new_status(1, dev) if _STATUS_CHECKS else None
     with torch.cuda.device(dev):
         check(lib.asu_kv_resolver_do(
             _stream(token_state), topk.data_ptr(), n, token_state.data_ptr(), record.data_ptr(),
             hbm_slot_of_token.data_ptr(), slot_owner_token.data_ptr(), stack.data_ptr(), free_slot_count.data_ptr(),
             stack.numel(), block_table.data_ptr(), block_table.numel(), o0.data_ptr(), o1.data_ptr(),
             m0.data_ptr(), m1.data_ptr(), rb0, rb1, src_rows, slot_count, max_seq, actual_seq_len, block_size,
-            resolved.data_ptr(), ws.data_ptr(), status.data_ptr()), "npu_asu_resolve_kv_slots_single_req")
-    _raise_on_status(status, "npu_asu_resolve_kv_slots_single_req", ignore=0)
+            resolved.data_ptr(), ws.data_ptr(), None if status is None else status.data_ptr()),
+            "npu_asu_resolve_kv_slots_single_req")
+    if status is not None:
+        _raise_on_status(status, "npu_asu_resolve_kv_slots_single_req", ignore=0)
     return resolved
 
 

@@ -102,7 +102,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--prefill", type=int, default=8)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    p.add_argument("--workload", choices=("resolver", "lru1", "lookup", "multilayer", "stress", "stress-block"),
+    p.add_argument("--workload", choices=("resolver", "lru1", "lookup", "multilayer", "stress", "stress-block", "decode"),
                    default="resolver")
     p.add_argument("--seed", type=int, default=2026)
     p.add_argument("--cpu-sample-s", type=float, default=12.0)
@@ -606,6 +606,212 @@ def run_lookup(args, world: int, rank: int, local_rank: int):
         print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ single-request decode resolver
+
+DECODE_LAYERS = 61          # attention layers of a DeepSeek-V3.2-class DSA decoder
+DECODE_MAX_SEQ = 131072
+DECODE_BLOCK = 128
+DECODE_TOPK = 2048
+DECODE_ROW0 = 512           # kv0 (latent) bf16 elements per token
+DECODE_ROW1 = 64            # kv1 (rope) bf16 elements per token
+
+
+def run_decode(args, world: int, rank: int, local_rank: int):
+    """One decode step of one request through `npu_asu_resolve_kv_slots_single_req` for every layer.
+
+    Per GPU one independent request (weak scaling): a 128K-token context whose first
+    `prefix` tokens are ASU-managed (ASU_ONLY) and whose tail is in the paged cache, a
+    per-layer top-k of 2048 (70% reuse + Zipf 1.1 locality; the newest token always
+    included), bf16 KV rows of 512 + 64 elements copied paged cache -> managed cache on a
+    miss, managed slots = max_seq_len (the manager's default).  After every step the
+    request appends one decode token.
+    """
+    import torch
+
+    import asu_ascend_b200
+
+    asu_ascend_b200.load()
+    from asu_ascend_b200 import manager as M
+    from asu_ascend_b200.dist import max_over_ranks
+    from asu_ascend_b200.workloads import FastLocalityTrace
+    from oracle import asu_oracle as O
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L, bs, K = DECODE_LAYERS, DECODE_BLOCK, args.steps
+    base = args.prefill + args.warmup
+    n_steps = base + 2 * K
+    if n_steps > 4096:
+        raise SystemExit("decode workload: prefill + warmup + 2 x steps must stay below 4096")
+    actual0 = DECODE_MAX_SEQ - n_steps - 28
+    prefix = (actual0 // bs) * bs
+    nblk = DECODE_MAX_SEQ // bs
+    g = torch.Generator(device=dev).manual_seed(args.seed + rank)
+    phys = nblk + 64
+    caches, bts = {}, []
+    for layer in range(L):
+        kv0 = torch.randn((phys, bs, 1, DECODE_ROW0), device=dev, generator=g, dtype=torch.bfloat16)
+        kv1 = torch.randn((phys, bs, 1, DECODE_ROW1), device=dev, generator=g, dtype=torch.bfloat16)
+        caches[f"layers.{layer}.self_attn"] = (kv0, kv1)
+    bt = torch.randperm(phys, device=dev, generator=g)[:nblk].to(torch.int32).reshape(1, nblk)
+    mgr = M.ASUFullKVCacheManagerFunctional.from_kv_caches(caches, DECODE_MAX_SEQ, bs, enabled=True)
+    mgr.reset_single_request(f"decode-req-{rank}", actual0, prefix, bt)
+    ctxs = [mgr.get_layer_context(f"layers.{layer}.self_attn") for layer in range(L)]
+    views = [c.original_kv_cache_views(caches[c.layer_name]) for c in ctxs]
+    # per-layer traces over the initial context; the newest token replaces the last entry
+    tr = FastLocalityTrace(L, actual0, topk=DECODE_TOPK, reuse=0.7, zipf_s=1.1, seed=args.seed + 31 * rank)
+    trace = np.stack([tr.step() for _ in range(n_steps)]).astype(np.int32)  # [step, layer, topk]
+    for i in range(n_steps):
+        trace[i, :, -1] = actual0 + i - 1
+    topk_dev = torch.from_numpy(trace).to(dev)
+    topk_host = torch.from_numpy(trace).pin_memory()
+    topk_buf = torch.empty((L, 1, 1, DECODE_TOPK), dtype=torch.int32, device=dev)
+    out_host = torch.empty((L, 1, 1, DECODE_TOPK), dtype=torch.int32, pin_memory=True)
+    op = torch.ops._C_ascend.npu_asu_resolve_kv_slots_single_req
+
+    def resolve_layer(layer, topk, seq):
+        c = ctxs[layer]
+        o0, o1 = views[layer]
+        return op(topk, seq, c.managed_prefix_len, c.token_state, c.asu_record_addr, c.hbm_slot_of_token,
+                  c.slot_owner_token, c.free_slot_stack, c.free_slot_count, bt, o0, o1, c.managed_kv_cache_0,
+                  c.managed_kv_cache_1, bs)
+
+    seq = actual0
+    step = 0
+    last = [None] * L
+
+    def advance():
+        nonlocal seq, step
+        mgr.mark_decode_token(seq)
+        seq += 1
+        step += 1
+
+    for _ in range(base):
+        for layer in range(L):
+            resolve_layer(layer, topk_dev[step, layer].reshape(1, 1, -1), seq)
+        advance()
+    torch.cuda.synchronize()
+    flush = L2Flush(torch, dev)
+    # enqueue time of one step's L calls (host side), to size the pre-queued sleep
+    t0 = time.perf_counter()
+    for layer in range(L):
+        resolve_layer(layer, topk_dev[step - 1, layer].reshape(1, 1, -1), seq)  # all hits: state unchanged
+    torch.cuda.synchronize()
+    enqueue_s = time.perf_counter() - t0
+    sleep_cycles = int(min(2.0 * enqueue_s, 0.2) * 2.0e9) + 200_000
+    free_before = torch.stack([c.free_slot_count for c in ctxs]).sum().item()
+    ms, ms_e2e = [], []
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(gpu_index(local_rank))
+    clocks.start()
+    for k in range(K):
+        flush()
+        torch.cuda._sleep(sleep_cycles)
+        a.record()
+        for layer in range(L):
+            last[layer] = resolve_layer(layer, topk_dev[step, layer].reshape(1, 1, -1), seq)
+        b.record()
+        b.synchronize()
+        ms.append(a.elapsed_time(b))
+        advance()
+    free_mid = torch.stack([c.free_slot_count for c in ctxs]).sum().item()
+    for k in range(K):
+        flush()
+        torch.cuda.synchronize()
+        a.record()
+        topk_buf.copy_(topk_host[step].reshape(L, 1, 1, -1), non_blocking=True)
+        outs = [resolve_layer(layer, topk_buf[layer], seq) for layer in range(L)]
+        for layer in range(L):
+            out_host[layer].copy_(outs[layer], non_blocking=True)
+        b.record()
+        b.synchronize()
+        ms_e2e.append(a.elapsed_time(b))
+        advance()
+    clock_info = clocks.stop()
+    installs_timed = free_before - free_mid
+    # parity: replay layer 0 through the oracle (states, slots, last outputs) and check the
+    # managed rows of every resident token of layer 0 against its paged-cache rows
+    c0 = ctxs[0]
+    ts, rec, hs, own, stack, cnt = O.reset_state(DECODE_MAX_SEQ, c0.managed_slot_count, bs, actual0, prefix,
+                                                 bt.cpu().numpy())
+    src0 = np.zeros((phys * bs, 1), np.uint8)
+    dst0 = np.zeros((c0.managed_slot_count, 1), np.uint8)
+    s_ = actual0
+    ref_out = None
+    for i in range(step):
+        ref_out = O.resolve_kv_slots_single_req(trace[i, 0].reshape(1, 1, -1), s_, ts, rec, hs, own, stack, cnt,
+                                                bt.cpu().numpy(), src0, src0, dst0, dst0, bs)
+        ts[s_] = O.TAIL_HBM
+        s_ += 1
+    if not (np.array_equal(c0.token_state.cpu().numpy(), ts) and np.array_equal(c0.hbm_slot_of_token.cpu().numpy(), hs)
+            and np.array_equal(c0.slot_owner_token.cpu().numpy(), own) and int(c0.free_slot_count.item()) == int(cnt[0])
+            and np.array_equal(outs[0].cpu().numpy(), ref_out)):
+        raise RuntimeError("decode resolver state differs from the oracle")
+    resident = torch.nonzero(c0.token_state == O.HBM_RESIDENT).reshape(-1)
+    paged = bt.reshape(-1).long()[resident // bs] * bs + resident % bs
+    slots_r = c0.hbm_slot_of_token[resident].long()
+    o0, o1 = views[0]
+    if not (torch.equal(c0.managed_kv_cache_0[slots_r], o0[paged]) and torch.equal(c0.managed_kv_cache_1[slots_r], o1[paged])):
+        raise RuntimeError("managed KV rows differ from the paged-cache rows")
+    tot_ms, tot_e2e = max_over_ranks([sum(ms), sum(ms_e2e)], dev)
+    if rank != 0:
+        return
+    # CPU leg: the Python restatement of the reference resolver on layer-0-sized state, with
+    # real 1,024 + 128-byte row copies, over the timed steps' top-k (~cpu-sample-s of work)
+    rows = phys * bs
+    src_a = np.zeros((rows, DECODE_ROW0), np.uint16)
+    src_b = np.zeros((rows, DECODE_ROW1), np.uint16)
+    dst_a = np.zeros((c0.managed_slot_count, DECODE_ROW0), np.uint16)
+    dst_b = np.zeros((c0.managed_slot_count, DECODE_ROW1), np.uint16)
+    st = O.reset_state(DECODE_MAX_SEQ, c0.managed_slot_count, bs, actual0, prefix, bt.cpu().numpy())
+    s_ = actual0
+    for i in range(base):
+        O.resolve_kv_slots_single_req(trace[i, 0].reshape(1, 1, -1), s_, *st, bt.cpu().numpy(), src_a, src_b,
+                                      dst_a, dst_b, bs)
+        st[0][s_] = O.TAIL_HBM
+        s_ += 1
+    calls, t0 = 0, time.perf_counter()
+    for i in range(base, base + K):
+        O.resolve_kv_slots_single_req(trace[i, 0].reshape(1, 1, -1), s_, *st, bt.cpu().numpy(), src_a, src_b,
+                                      dst_a, dst_b, bs)
+        st[0][s_] = O.TAIL_HBM
+        s_ += 1
+        calls += 1
+        if time.perf_counter() - t0 > args.cpu_sample_s:
+            break
+    cpu_s = time.perf_counter() - t0
+    idx = world * L * DECODE_TOPK * K
+    p50 = statistics.median(ms)
+    value = idx / (tot_ms * 1e-3)
+    line = base_line(world, K, args.warmup, tot_ms / K, value,
+                     {"workload": f"decode: 1 request/GPU, {L} layers x npu_asu_resolve_kv_slots_single_req, "
+                                  f"max_seq {DECODE_MAX_SEQ}, context {actual0}..{actual0 + n_steps} "
+                                  f"(ASU prefix {prefix}), top-k {DECODE_TOPK} (70% reuse + zipf 1.1, newest "
+                                  f"token included), bf16 rows {DECODE_ROW0}+{DECODE_ROW1}, block {bs}, "
+                                  f"{c0.managed_slot_count} managed slots/layer", "l2": L2_NOTE})
+    hbm = float(load_peaks().get("hbm_gbs", 6650.0))
+    per_inst = 2 * (2 * DECODE_ROW0 + 2 * DECODE_ROW1) + 4 * 6
+    alg = (installs_timed / K) * per_inst + L * DECODE_TOPK * 16
+    achieved = alg / (p50 * 1e-3) / 1e9
+    line.update({
+        "p50_step_us": p50 * 1e3, "p50_call_us": p50 * 1e3 / L,
+        "installs_per_step": installs_timed / K, "miss_rate": installs_timed / (K * L * DECODE_TOPK),
+        "roofline": {"bound": "hbm", "kernel": "resolve_kernel + resolver_copy_kernel (per layer)",
+                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                     "algorithmic_bytes_per_step": alg,
+                     "note": "latency-bound: one CTA resolves a 2048-entry top-k; bytes per step are small"},
+        "e2e": {"value": idx / (tot_e2e * 1e-3), "unit": UNIT, "h2d_bytes_per_step": L * DECODE_TOPK * 4,
+                "d2h_bytes_per_step": L * DECODE_TOPK * 4,
+                "note": "top-k of all layers copied in, resolved slots copied out, host dispatch of the op included"},
+        "gpu_launches": 2 * L * K,
+        "cpu_baseline": {"value": calls * DECODE_TOPK / cpu_s, "unit": UNIT, "cores": 1, "kind": "port",
+                         "sample": f"{calls} layer-0 calls of the Python restatement of the reference resolver "
+                                   f"(patch/0001 asu_kv_resolver.py) with real row copies"},
+        "clocks": clock_info,
+    })
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -625,6 +831,8 @@ def main():
             run_resolver(args, RESOLVER_WORKLOADS[args.workload], world, rank, local_rank)
         elif args.workload == "lru1":
             run_lru1(args, world, rank, local_rank)
+        elif args.workload == "decode":
+            run_decode(args, world, rank, local_rank)
         else:
             run_lookup(args, world, rank, local_rank)
     finally:

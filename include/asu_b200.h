@@ -214,6 +214,18 @@ int asu_kv_resolver_do(void* stream, const int32_t* topk, int64_t topk_numel, in
 
 int64_t asu_kv_resolver_workspace_bytes(int64_t topk_numel);
 
+/* Replaces ASULayerKVCacheContext.reset_state (patch/0003 asu_kv_cache_manager.py, patch lines
+ * 234-292) with one launch: token_state / asu_record_addr / hbm_slot_of_token [max_seq_len] and
+ * slot_owner_token [slot_count] reset to INVALID, free_slot_stack = 0..slot_count-1,
+ * free_slot_count = slot_count; positions below managed_prefix_len become ASU_ONLY with
+ * record block_table[p/block_size]*block_size + p%block_size, positions up to actual_seq_len
+ * TAIL_HBM.  Rejects (ASU_ERR_ARG) the lengths the reference raises on. */
+int asu_resolver_reset(void* stream, int32_t* token_state, int32_t* asu_record_addr, int32_t* hbm_slot_of_token,
+                       int64_t max_seq_len, int32_t* slot_owner_token, int32_t* free_slot_stack,
+                       int32_t* free_slot_count, int64_t slot_count, const int32_t* block_table,
+                       int64_t block_table_len, int64_t block_size, int64_t actual_seq_len,
+                       int64_t managed_prefix_len);
+
 /* No counterpart in the reference.  The same resolver as asu_kv_resolver_do, for callers that
  * cannot allocate device memory while resolving (an engine whose HBM is pre-reserved for its
  * KV-block pool and that forbids cudaMalloc in the decode loop; a C / FFI host without a
