@@ -201,7 +201,9 @@ int asu_host_pool_free(void* host_ptr);
  * Serial semantics over topk[0..topk_numel): HBM_RESIDENT -> hbm_slot_of_token; ASU_ONLY /
  * TAIL_HBM -> pop free_slot_stack[--free_slot_count], copy the KV row pair from source row
  * (asu_record_addr[tok], or block_table[tok/block_size]*block_size + tok%block_size) to the
- * popped managed slot, then mark resident.  kv rows are raw bytes (kv*_row_bytes each).
+ * popped managed slot, then mark resident.  kv rows are raw bytes (kv*_row_bytes each,
+ * kv0_row_bytes + kv1_row_bytes <= 1 MiB).  On return `workspace` holds the install list:
+ * int32 count, then (source row, managed slot) pairs in install order.
  * `workspace` must hold asu_kv_resolver_workspace_bytes(topk_numel) bytes of device memory.
  * status: one int32 (nullable). */
 int asu_kv_resolver_do(void* stream, const int32_t* topk, int64_t topk_numel, int32_t* token_state,

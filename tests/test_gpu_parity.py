@@ -553,6 +553,72 @@ def test_resolver_second_resolve_is_idempotent():
         assert torch.equal(m0[slot], kv0[src]) and torch.equal(m1[slot], kv1[src])
 
 
+@pytest.mark.parametrize("n,key_range,seed", [(6000, 3000, 21), (4097, 100000, 22), (2049, 40, 23)])
+def test_resolver_multi_chunk_duplicates_match_oracle(n, key_range, seed):
+    """Top-k longer than one 2048-entry chunk, duplicates inside and across chunks, all three
+    token states in play: outputs, state arrays, free count and managed rows equal the serial
+    oracle's."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    max_seq, slots, bs = 131072, 8192, 128
+    actual = key_range + 500 if key_range + 500 <= max_seq else max_seq
+    prefix = actual - 300
+    nblk = (max_seq + bs - 1) // bs
+    bt = rng.permutation(nblk + 16)[:nblk].astype(np.int32)
+    ts, rec, hs, own, stack, cnt = O.reset_state(max_seq, slots, bs, actual, prefix, bt)
+    # some tokens already resident
+    warm = rng.choice(actual, 500, replace=False).astype(np.int32)
+    src0 = rng.integers(0, 256, ((nblk + 16) * bs, 48), dtype=np.uint8)
+    src1 = rng.integers(0, 256, ((nblk + 16) * bs, 16), dtype=np.uint8)
+    dst0 = np.zeros((slots, 48), np.uint8)
+    dst1 = np.zeros((slots, 16), np.uint8)
+    O.resolve_kv_slots_single_req(warm.reshape(1, -1), actual, ts, rec, hs, own, stack, cnt, bt, src0, src1, dst0,
+                                  dst1, bs)
+    tts, trec, ths, town, tstack, tcnt = T(ts), T(rec), T(hs), T(own), T(stack), T(cnt)
+    m0, m1 = T(dst0), T(dst1)
+    lo = max(0, actual - key_range)
+    topk = rng.integers(lo, actual, (1, 3, (n + 2) // 3)).astype(np.int32)
+    topk.reshape(-1)[-1] = actual - 1
+    exp = O.resolve_kv_slots_single_req(topk, actual, ts, rec, hs, own, stack, cnt, bt, src0, src1, dst0, dst1, bs)
+    out = torch.ops._C_ascend.npu_asu_resolve_kv_slots_single_req(
+        T(topk), actual, prefix, tts, trec, ths, town, tstack, tcnt, T(bt), T(src0).view(torch.bfloat16),
+        T(src1).view(torch.bfloat16), m0.view(torch.bfloat16), m1.view(torch.bfloat16), bs)
+    np.testing.assert_array_equal(N(out), exp)
+    np.testing.assert_array_equal(N(tts), ts)
+    np.testing.assert_array_equal(N(ths), hs)
+    np.testing.assert_array_equal(N(town), own)
+    assert int(N(tcnt).reshape(-1)[0]) == int(cnt[0])
+    np.testing.assert_array_equal(N(m0), dst0)
+    np.testing.assert_array_equal(N(m1), dst1)
+
+
+@pytest.mark.parametrize("w0,w1", [(3, 5), (2, 6), (8, 0)])
+def test_resolver_row_widths_match_oracle(w0, w1):
+    """fp16 rows of 6/10 bytes (byte copies), 4/12 bytes (4-byte copies) and 16 bytes with an
+    empty second cache: the managed rows equal the oracle's byte for byte."""
+    rng = np.random.Generator(np.random.PCG64(w0 * 10 + w1))
+    max_seq, slots, bs, actual, prefix = 4096, 3000, 16, 4000, 3900
+    nblk = max_seq // bs
+    bt = rng.permutation(nblk + 4)[:nblk].astype(np.int32)
+    ts, rec, hs, own, stack, cnt = O.reset_state(max_seq, slots, bs, actual, prefix, bt)
+    src0 = rng.integers(0, 1 << 16, ((nblk + 4) * bs, w0), dtype=np.uint16)
+    src1 = rng.integers(0, 1 << 16, ((nblk + 4) * bs, w1), dtype=np.uint16)
+    dst0 = np.zeros((slots, w0), np.uint16)
+    dst1 = np.zeros((slots, w1), np.uint16)
+    tts, trec, ths, town, tstack, tcnt = T(ts), T(rec), T(hs), T(own), T(stack), T(cnt)
+    m0, m1 = T(dst0.view(np.int16)), T(dst1.view(np.int16))
+    for step in range(2):
+        topk = rng.integers(0, actual, (1, 2500)).astype(np.int32)
+        exp = O.resolve_kv_slots_single_req(topk, actual, ts, rec, hs, own, stack, cnt, bt, src0, src1, dst0, dst1,
+                                            bs)
+        out = torch.ops._C_ascend.npu_asu_resolve_kv_slots_single_req(
+            T(topk), actual, prefix, tts, trec, ths, town, tstack, tcnt, T(bt), T(src0.view(np.int16)).view(torch.float16),
+            T(src1.view(np.int16)).view(torch.float16), m0.view(torch.float16), m1.view(torch.float16), bs)
+        np.testing.assert_array_equal(N(out), exp)
+        np.testing.assert_array_equal(N(m0).view(np.uint16), dst0)
+        np.testing.assert_array_equal(N(m1).view(np.uint16), dst1)
+        assert int(N(tcnt).reshape(-1)[0]) == int(cnt[0])
+
+
 def test_resolver_errors_are_reported():
     from asu_ascend_b200._lib import AsuError
 
