@@ -1,0 +1,94 @@
+"""FlashMLA-sparse decode fed by resolver slots (the B200 counterpart of the reference's
+patch/0004 decode parity case, patch lines 265-293): attention over (managed cache, resolved
+slots) equals attention over (paged cache, block-table slots) within 2e-2, and resolving the
+same top-k again consumes no slot and returns the same slots."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import asu_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def _paged_slots(topk, bt, bs):
+    """vLLM's triton_convert_req_index_to_global_index for one request (sparse_utils.py:97-105)."""
+    t = topk.long()
+    return torch.where(t >= 0, bt.long()[t.clamp(min=0) // bs] * bs + t.clamp(min=0) % bs, -1).to(torch.int32)
+
+
+def _case(seed, seq, bs=64, tokens=2, topk=2048, pad=0, row=576, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    nblk = (seq + bs - 1) // bs
+    phys = nblk + 8
+    if dtype == torch.uint8:
+        kv = torch.randint(0, 256, (phys, bs, row), generator=g, dtype=torch.uint8)
+    else:
+        kv = (torch.randn(phys, bs, row, generator=g) * 0.5).to(dtype)
+    bt = torch.randperm(phys, generator=g)[:nblk].to(torch.int32)
+    k = min(seq, topk - pad)  # distinct positions per query token, then -1 padding
+    idx = torch.full((tokens, topk), -1, dtype=torch.int32)
+    for i in range(tokens):
+        idx[i, :k] = torch.randperm(seq, generator=g)[:k].to(torch.int32)
+    return kv.to(DEV), bt.to(DEV), idx.to(DEV)
+
+
+@pytest.mark.parametrize("seq,pad", [(4133, 0), (1500, 2048 - 1500)])
+def test_flashmla_sparse_decode_on_managed_cache_matches_paged(seq, pad):
+    fm = pytest.importorskip("vllm.third_party.flashmla.flash_mla_interface")
+    from asu_ascend_b200 import sparse_mla as S
+
+    kv, bt, topk = _case(3, seq, pad=pad)
+    q = (torch.randn(topk.shape[0], 128, 576, generator=torch.Generator().manual_seed(9)) * 0.5).to(torch.bfloat16)
+    q = q.to(DEV)
+    scale = 576 ** -0.5
+    origin = fm.flash_mla_sparse_fwd(q, kv.view(-1, 1, 576), _paged_slots(topk, bt, 64).view(2, 1, -1), scale)[0]
+
+    mgr = S.contexts_for_mla({"layers.0.self_attn": kv}, max_seq_len=seq, block_size=64, managed_slot_count=8192,
+                             enabled=True)
+    mgr.reset_single_request("decode-req-0", seq, seq - 37, bt)
+    ctx = mgr.get_layer_context("layers.0.self_attn")
+    out = S.sparse_mla_decode(q, ctx, topk, bt, kv, scale)
+    torch.testing.assert_close(out.float(), origin.float(), rtol=2e-2, atol=2e-2)
+
+    slots = S.resolve_topk(ctx, topk, bt, kv)  # all resident now
+    left = int(ctx.free_slot_count.item())
+    again = S.resolve_topk(ctx, topk, bt, kv)
+    assert int(ctx.free_slot_count.item()) == left
+    assert torch.equal(again, slots)
+    assert bool((slots[topk < 0] == -1).all())
+    valid = topk >= 0
+    assert torch.equal(ctx.managed_kv_cache_0[slots[valid].long()],
+                       kv.view(-1, 576)[_paged_slots(topk, bt, 64)[valid].long()])
+
+
+def test_resolve_topk_fp8_ds_mla_rows_match_oracle():
+    """656-byte fp8_ds_mla rows (uint8 cache): slots, state and row bytes equal the oracle's."""
+    from asu_ascend_b200 import sparse_mla as S
+
+    seq, bs = 6000, 64
+    kv, bt, topk = _case(5, seq, tokens=1, topk=2048, pad=100, row=656, dtype=torch.uint8)
+    mgr = S.contexts_for_mla({"l": kv}, max_seq_len=seq, block_size=bs, managed_slot_count=4096, enabled=True)
+    mgr.reset_single_request("r", seq, seq - 20, bt)
+    ctx = mgr.get_layer_context("l")
+    ctx.managed_kv_cache_0.zero_()
+    ts, rec, hs, own, stack, cnt = O.reset_state(seq, 4096, bs, seq, seq - 20, bt.cpu().numpy())
+    src = kv.view(-1, 656).cpu().numpy()
+    dst = np.zeros((4096, 656), np.uint8)
+    empty_src = np.zeros((src.shape[0], 0), np.uint8)
+    empty_dst = np.zeros((4096, 0), np.uint8)
+    t = topk.cpu().numpy()[0]
+    valid = t[t >= 0]
+    exp = O.resolve_kv_slots_single_req(valid.reshape(1, -1), seq, ts, rec, hs, own, stack, cnt, bt.cpu().numpy(),
+                                        src, empty_src, dst, empty_dst, bs)
+    out = S.resolve_topk(ctx, topk, bt, kv)
+    got = out.cpu().numpy()[0]
+    np.testing.assert_array_equal(got[t >= 0], exp.reshape(-1))
+    assert (got[t < 0] == -1).all()
+    np.testing.assert_array_equal(ctx.token_state.cpu().numpy(), ts)
+    np.testing.assert_array_equal(ctx.slot_owner_token.cpu().numpy(), own)
+    assert int(ctx.free_slot_count.item()) == int(cnt[0])
+    np.testing.assert_array_equal(ctx.managed_kv_cache_0.cpu().numpy(), dst)

@@ -69,3 +69,24 @@ def test_reset_argument_errors_match_the_reference():
         ctx.reset_state("r", 6, 4, bt)
     with pytest.raises(RuntimeError):
         ctx.mark_decode_token(8)
+
+
+def test_sparse_mla_contexts_have_one_managed_cache():
+    from asu_ascend_b200 import sparse_mla as S
+
+    caches = {"layers.0.self_attn": torch.zeros((3, 64, 576), dtype=torch.bfloat16),
+              "layers.1.self_attn": torch.zeros((3, 64, 656), dtype=torch.uint8),
+              "indexer": torch.zeros((3, 64))}
+    mgr = S.contexts_for_mla(caches, max_seq_len=192, block_size=64, managed_slot_count=50, enabled=True)
+    assert mgr.has_layer("layers.0.self_attn") and mgr.has_layer("layers.1.self_attn") and not mgr.has_layer("indexer")
+    c0 = mgr.get_layer_context("layers.0.self_attn")
+    assert c0.managed_kv_cache_0.shape == (50, 576) and c0.managed_kv_cache_1.numel() == 0
+    assert S.managed_kv_view(c0).shape == (50, 1, 576)
+    c1 = mgr.get_layer_context("layers.1.self_attn")
+    assert c1.managed_kv_cache_0.dtype == torch.uint8 and c1.managed_kv_cache_0.shape == (50, 656)
+    with pytest.raises(RuntimeError, match="int32"):
+        S.resolve_topk(c0, torch.zeros((1, 8), dtype=torch.int64), torch.zeros(3, dtype=torch.int32),
+                       caches["layers.0.self_attn"])
+    with pytest.raises(RuntimeError, match="rows"):
+        S.resolve_topk(c0, torch.zeros((1, 8), dtype=torch.int32), torch.zeros(3, dtype=torch.int32),
+                       caches["layers.1.self_attn"])
