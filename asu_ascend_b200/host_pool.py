@@ -90,5 +90,54 @@ class HostRowPool:
                 R, None if status is None else status.data_ptr()), "asu_swapin_gather")
 
 
+    def writeback(self, src: torch.Tensor, dst_rows: torch.Tensor, src_index: torch.Tensor | None = None,
+                  status: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> None:
+        """pool[dst_rows[i]] = src[src_index[i] if given else i] (the producer side of ``swapin``).
+
+        ``src`` is a CUDA tensor of rows of ``row_bytes`` bytes (any dtype, rows contiguous);
+        negative ``dst_rows`` entries are skipped.  Asynchronous: synchronize ``stream`` before
+        reading the rows on the host."""
+        dev = src.device
+        if src.device.type != "cuda" or src.dim() < 2 or not src.is_contiguous():
+            raise RuntimeError("src must be a contiguous [n, ...] CUDA tensor")
+        row = src[0].numel() * src.element_size()
+        if row != self.row_bytes:
+            raise RuntimeError(f"src rows are {row} bytes, the host pool's are {self.row_bytes}")
+        for name, t in (("dst_rows", dst_rows), ("src_index", src_index)):
+            if t is not None and (t.dtype != torch.int32 or t.device != dev or not t.is_contiguous()):
+                raise RuntimeError(f"{name} must be a contiguous int32 CUDA tensor on {dev}")
+        n = dst_rows.numel()
+        if src_index is None and n > src.shape[0]:
+            raise RuntimeError("dst_rows has more entries than src has rows")
+        if src_index is not None and src_index.numel() != n:
+            raise RuntimeError("src_index and dst_rows must have the same length")
+        s = (stream or torch.cuda.current_stream(dev)).cuda_stream
+        with torch.cuda.device(dev):
+            check(lib.asu_host_pool_writeback(
+                s, self.device_ptr, self.rows, self.row_bytes, self.pitch, src.data_ptr(), src.shape[0], row,
+                None if src_index is None else src_index.data_ptr(), dst_rows.data_ptr(), n,
+                None if status is None else status.data_ptr()), "asu_host_pool_writeback")
+
+
+    def writeback_range(self, src: torch.Tensor, first_row: int, status: torch.Tensor | None = None,
+                        stream: torch.cuda.Stream | None = None) -> None:
+        """pool[first_row + i] = src[i] for every row of ``src``: a contiguous range of host rows,
+        with no row-index tensor."""
+        dev = src.device
+        if src.device.type != "cuda" or src.dim() < 2 or not src.is_contiguous():
+            raise RuntimeError("src must be a contiguous [n, ...] CUDA tensor")
+        row = src[0].numel() * src.element_size()
+        if row != self.row_bytes:
+            raise RuntimeError(f"src rows are {row} bytes, the host pool's are {self.row_bytes}")
+        n = src.shape[0]
+        if first_row < 0 or first_row + n > self.rows:
+            raise RuntimeError("row range exceeds the pool")
+        s = (stream or torch.cuda.current_stream(dev)).cuda_stream
+        with torch.cuda.device(dev):
+            check(lib.asu_host_pool_writeback(
+                s, self.device_ptr + first_row * self.pitch, n, self.row_bytes, self.pitch, src.data_ptr(), n, row,
+                None, None, n, None if status is None else status.data_ptr()), "asu_host_pool_writeback")
+
+
 def check_status(status: torch.Tensor, what: str, ignore: int = 0) -> None:
     raise_on_status(status, what, ignore)

@@ -22,6 +22,8 @@ Other workloads (`--workload`):
   stress        128 requests, 1M-token context, top-k 2048, 20% reuse + uniform draws
   stress-block  the stress context in 64-token blocks: top-k 32 blocks, 128 block slots,
                 41,984-byte rows
+  decode        1 request, 61 layers x npu_asu_resolve_kv_slots_single_req per decode step
+  writeback     prefill write-back of a 128K-token context x 4 layers into the pinned pool
 All inputs are synthetic and seeded.
 
 Prints one JSON line (rank 0).  `value` is resolved indices/s for the whole job with inputs
@@ -102,7 +104,8 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--prefill", type=int, default=8)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    p.add_argument("--workload", choices=("resolver", "lru1", "lookup", "multilayer", "stress", "stress-block", "decode"),
+    p.add_argument("--workload", choices=("resolver", "lru1", "lookup", "multilayer", "stress", "stress-block", "decode",
+                            "writeback"),
                    default="resolver")
     p.add_argument("--seed", type=int, default=2026)
     p.add_argument("--cpu-sample-s", type=float, default=12.0)
@@ -277,10 +280,13 @@ def run_reference(args, world: int, rank: int):
 
 # ------------------------------------------------------------------ GPU helpers
 
-def h2d_peak_gbs(torch, dev) -> float:
+def h2d_peak_gbs(torch, dev, d2h: bool = False) -> float:
+    """Best of 10 pinned 256 MiB cudaMemcpyAsync copies (host -> device, or device -> host)."""
     n = 256 << 20
     src = torch.empty(n, dtype=torch.uint8, pin_memory=True)
     dst = torch.empty(n, dtype=torch.uint8, device=dev)
+    if d2h:
+        src, dst = dst, src
     best = 0.0
     for _ in range(10):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -825,6 +831,99 @@ def run_decode(args, world: int, rank: int, local_rank: int):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ host-pool producer
+
+WB_TOKENS = 131072
+WB_LAYERS = 4
+
+
+def run_writeback(args, world: int, rank: int, local_rank: int):
+    """Prefill write-back: each step stores one request's 128K-token context of 656-byte rows for
+    4 layers from HBM into the pinned host pool (HostKVStore.write_back, one launch per layer),
+    the producer side of the swap-in.  Per GPU one request per step (weak scaling)."""
+    import torch
+
+    import asu_ascend_b200
+
+    asu_ascend_b200.load()
+    from asu_ascend_b200 import kv_store as KV
+    from asu_ascend_b200.dist import max_over_ranks
+    from asu_ascend_b200.host_pool import HostRowPool
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    row, L, T = 656, WB_LAYERS, WB_TOKENS
+    pool = HostRowPool(rows=2 * L * T, row_bytes=row)
+    store = KV.HostKVStore(pool.array, tokens_per_extent=T, pool=pool)
+    g = torch.Generator(device=dev).manual_seed(args.seed + rank)
+    src = [torch.randint(0, 256, (T, row), dtype=torch.uint8, device=dev, generator=g) for _ in range(L)]
+    flush = L2Flush(torch, dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def step(k):
+        req = f"prefill-{rank}-{k % 2}"  # two requests alternate over the pool's two halves
+        for layer in range(L):
+            store.write_back(KV.KV_MLA_TOKEN, req, layer, 0, src[layer])
+
+    for k in range(args.warmup):
+        step(k)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(gpu_index(local_rank))
+    clocks.start()
+    ms = []
+    for k in range(args.steps):
+        flush()
+        torch.cuda._sleep(200_000)
+        a.record()
+        step(k)
+        b.record()
+        b.synchronize()
+        ms.append(a.elapsed_time(b))
+    clock_info = clocks.stop()
+    # the last step's request: every key of layer 3 holds its source row
+    last = f"prefill-{rank}-{(args.steps - 1) % 2}"
+    check = np.random.default_rng(1).integers(0, T, 64)
+    host = src[L - 1].cpu().numpy()
+    for t in check:
+        if store.get(KV.KV_MLA_TOKEN, KV.make_key(last, L - 1, int(t))) != host[t].tobytes():
+            raise RuntimeError("written-back row differs from its source")
+    tot_ms = max_over_ranks([sum(ms)], dev)[0]
+    if rank != 0:
+        pool.close()
+        return
+    peak = h2d_peak_gbs(torch, dev, d2h=True)
+    rows_per_step = L * T
+    p50 = statistics.median(ms)
+    achieved = rows_per_step * row / (p50 * 1e-3) / 1e9
+    cpu_rows, cpu_s = 0, 0.0
+    if not args.no_cpu_baseline:  # numpy row copy into the same host rows, one thread
+        hsrc = [x.cpu().numpy() for x in src]
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < min(args.cpu_sample_s, 5.0):
+            for layer in range(L):
+                base = store.extent_base(KV.KV_MLA_TOKEN, last, layer)  # rows the GPU steps wrote
+                pool.array[base:base + T] = hsrc[layer]
+                cpu_rows += T
+        cpu_s = time.perf_counter() - t0
+    line = base_line(world, args.steps, args.warmup, tot_ms / args.steps, world * rows_per_step * args.steps / (tot_ms * 1e-3),
+                     {"workload": f"writeback: 1 request/GPU per step, {T}-token prefill x {L} layers of {row}-byte "
+                                  f"rows written from HBM into the pinned host pool (MicroKV-keyed extents)",
+                      "l2": L2_NOTE})
+    line.update({"metric": "prefill KV rows written back per second (HBM -> pinned host pool)", "unit": "rows/s",
+                 "dtype": "u8", "p50_step_us": p50 * 1e3, "writeback_gbs": achieved,
+                 "roofline": {"bound": "host_link", "kernel": "writeback_kernel", "achieved": achieved, "peak": peak,
+                              "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                              "peak_note": "pinned 256 MiB device-to-host cudaMemcpyAsync, best of 10, same run"},
+                 "e2e": None, "gpu_launches": L * args.steps,
+                 "cpu_baseline": None if not cpu_rows else {
+                     "value": cpu_rows / cpu_s, "unit": "rows/s", "cores": 1, "kind": "port",
+                     "sample": "numpy copy of the same host-resident rows into the pool rows (the MicroKV "
+                               "batch_put path is a socket round trip and slower)"},
+                 "clocks": clock_info})
+    print(json.dumps(line), flush=True)
+    pool.close()
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -846,6 +945,8 @@ def main():
             run_lru1(args, world, rank, local_rank)
         elif args.workload == "decode":
             run_decode(args, world, rank, local_rank)
+        elif args.workload == "writeback":
+            run_writeback(args, world, rank, local_rank)
         else:
             run_lookup(args, world, rank, local_rank)
     finally:

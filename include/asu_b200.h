@@ -187,6 +187,18 @@ int asu_swapin_gather(void* stream, const void* host_pool, int64_t pool_rows, ui
                       const uint8_t* install_mask, uint32_t query_count, void* slot_pool, uint32_t slot_count,
                       uint32_t req_num, int32_t* status);
 
+/* Producer side of the swap-in: host_pool[dst_row ? dst_row[i] : i] = src[src_index ? src_index[i]
+ * : i] for i < n (rows of row_bytes; src rows src_pitch bytes apart in device memory, host rows
+ * host_pitch bytes apart, 0 = row_bytes); dst_row[i] < 0 skips item i.  Replaces the MicroKV
+ * batch_put of prefilled records (docs/v0.1/kv-cache-offload-v0.1-real-ops-design.md:243-292;
+ * MicroKV/python/microkv/client.py batch_put).  Out-of-range rows set ASU_ST_BAD_STATE (host
+ * row) or ASU_ST_BAD_SOURCE (source row) in status[0] (nullable) and are skipped.  row_bytes and
+ * both pitches must be multiples of 16, both pointers 16-byte aligned, and n * row_bytes / 16
+ * below 2^31 (split larger write-backs). */
+int asu_host_pool_writeback(void* stream, void* host_pool, int64_t pool_rows, uint32_t row_bytes,
+                            uint32_t host_pitch, const void* src, int64_t src_rows, uint64_t src_pitch,
+                            const int32_t* src_index, const int32_t* dst_row, int64_t n, int32_t* status);
+
 /* Pinned, mapped host allocation for the row pool (cudaHostAlloc Portable|Mapped). */
 int asu_host_pool_alloc(uint64_t bytes, void** host_ptr, void** device_ptr);
 int asu_host_pool_free(void* host_ptr);

@@ -385,9 +385,33 @@ def resolver_fixtures(res_mod, mgr_mod):
     np.savez_compressed(HERE / "resolver.npz", **arrays)
 
 
+# ---------------------------------------------------------------------------
+# MicroKV keys (MicroKV/python/microkv/client.py make_key)
+# ---------------------------------------------------------------------------
+
+MICROKV_KEY_CASES = [
+    ("req-phase1", 2, 0, 0), ("req-phase1", 2, 3, 0), ("shared-server", 0, 0, 0), ("mla-req", 12, 34, 0),
+    ("type-space", 1, 1, 2), ("", 0, 0, 0), ("\u8bf7\u6c42-7", 61, 131071, 3),
+    (0, 0, 0, 0), (1, 2, 3, 1), (0xFFFFFFFFFFFFFFFF, 0xFFFFFFFF, 0xFFFFFFFF, 255), (123456789, 60, 4095, 0),
+]
+
+
+def microkv_fixtures(client):
+    keys = [client.make_key(r, layer, pos, t) for r, layer, pos, t in MICROKV_KEY_CASES]
+    req_str = np.asarray([r if isinstance(r, str) else "" for r, *_ in MICROKV_KEY_CASES])
+    req_int = np.asarray([r if isinstance(r, int) else 0 for r, *_ in MICROKV_KEY_CASES], np.uint64)
+    is_str = np.asarray([isinstance(r, str) for r, *_ in MICROKV_KEY_CASES])
+    fields = np.asarray([c[1:] for c in MICROKV_KEY_CASES], np.int64)
+    np.savez_compressed(HERE / "microkv_keys.npz", keys=np.frombuffer(b"".join(keys), np.uint8).reshape(-1, 32),
+                        req_str=req_str, req_int=req_int, is_str=is_str, fields=fields)
+
+
 def main():
     if not REF.exists():
         raise SystemExit(f"reference not found at {REF}")
+    if sys.argv[1:] == ["microkv"]:  # only the MicroKV key fixture
+        microkv_fixtures(_load("microkv_client", REF / "MicroKV" / "python" / "microkv" / "client.py"))
+        return
     sim = _load("kv_cache_eviction_sim", REF / "simu" / "kv_cache_eviction_sim.py")
     common = _load("asu_hbm_index_common", REF / "ops" / "scripts" / "asu_hbm_index_common.py")
     common.np = np  # the module resolves numpy lazily through require_numpy()
@@ -411,6 +435,7 @@ def main():
     ops_fixtures(common)
     batch_lru_fixtures(ref_lru, ref_wl)
     gather_fixtures(tlu)
+    microkv_fixtures(_load("microkv_client", REF / "MicroKV" / "python" / "microkv" / "client.py"))
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 
