@@ -31,9 +31,11 @@ STATUS_BITS = {
     0x20: "BAD_SOURCE",
     0x40: "BAD_TOKEN_STATE",
     0x80: "NO_VICTIM",
+    0x100: "TIMEOUT",
 }
 ST_BAD_QUERY, ST_FREE_EXHAUSTED, ST_RING_EXHAUSTED, ST_BAD_STATE = 0x01, 0x02, 0x04, 0x08
 ST_SHORTAGE, ST_BAD_SOURCE, ST_BAD_TOKEN_STATE, ST_NO_VICTIM = 0x10, 0x20, 0x40, 0x80
+ST_TIMEOUT = 0x100
 
 LRU_STAT_COLS = 5
 

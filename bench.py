@@ -112,7 +112,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--layers", type=int, default=61, help="decode workload: attention layers per step")
     p.add_argument("--host-pitch", type=int, default=0,
-                   help="bytes between host-pool rows (0: packed rows)")
+                   help="bytes between host-pool rows (0: the pool's default, rows up to 1 KiB padded "
+                        "to a multiple of 128 bytes)")
     return p.parse_args()
 
 

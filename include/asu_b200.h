@@ -44,6 +44,7 @@ extern "C" {
 #define ASU_ST_BAD_SOURCE 0x20      /* swap-in / resolver: source row out of range */
 #define ASU_ST_BAD_TOKEN_STATE 0x40 /* resolver: token_state not in {ASU_ONLY, HBM_RESIDENT, TAIL_HBM} */
 #define ASU_ST_NO_VICTIM 0x80       /* batch-LRU: more unique misses than evictable slots (state left unchanged) */
+#define ASU_ST_TIMEOUT 0x100        /* swap-in: a bulk copy did not complete within its wait limit (rows skipped) */
 
 /* ---- reference constants (ops/asu_hbm_index_lookup_aiv.cpp:7-12) ------- */
 #define ASU_HBM_INDEX_SIZE (128u * 1024u)
@@ -180,7 +181,9 @@ int asu_lru_step(void* stream, int32_t* token_to_slot, int32_t* slot_to_token, i
  * row_bytes; device-accessible mapped pinned memory) into slot_pool[r, slot[r,pos]]
  * ([req, slot_count, row_bytes], HBM).  Replaces the MicroKV batch_get + H2D of the v0.1 design
  * (docs/v0.1/kv-cache-offload-v0.1-real-ops-design.md:293-312).  row_bytes and host_pitch must
- * be multiples of 16 and both pools 16-byte aligned. */
+ * be multiples of 16 and both pools 16-byte aligned.  Rows up to 1 KiB move as one TMA bulk copy
+ * each (a host_pitch that is a multiple of 128 reads whole lines); a bulk copy that does not
+ * complete within its wait limit sets ASU_ST_TIMEOUT and its lane stops. */
 int asu_swapin_gather(void* stream, const void* host_pool, int64_t pool_rows, uint32_t row_bytes,
                       uint32_t host_pitch, const int32_t* record_addr, uint32_t key_space, const int32_t* query,
                       const int32_t* slot,
