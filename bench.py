@@ -59,8 +59,8 @@ METRIC = "resolved KV indices/sec (lookup + LRU maintain + swap-in gather)"
 # Ascend 910B (docs/archive/hbm_kvcache_lookup_recommendations.md:32) = 2.93e8 indices/s.
 REF_LOOKUP_IDX_PER_S = 50 * 2048 / 350e-6
 # From the ncu captures summarised in profiles/ (first timed step of the resolver workload):
-SWAPIN_PCIE_READ_BYTES_PER_LAUNCH = 52.49e9 * 714.4e-6   # pcie__read_bytes.sum.per_second x duration
-SWAPIN_NCU_INSTALLS = 31.0e6 / 656                        # rows swapped in by that launch (~31 MB)
+SWAPIN_PCIE_READ_BYTES_PER_LAUNCH = 54.31e9 * 652.4e-6   # pcie__read_bytes.sum.per_second x duration
+SWAPIN_NCU_INSTALLS = 0.182 * 128 * 2048                  # rows swapped in by that launch (~18.2% miss)
 LRU_DRAM_BYTES_PER_LAUNCH = 22.05e6 + 0.055e6             # dram__bytes_read.sum + dram__bytes_write.sum
 
 
@@ -454,11 +454,12 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             "p50_swapin_us": statistics.median(swapin_ms) * 1e3,
             "miss_rate": installs / (launches * R * cfg.topk),
             "swapin_gbs": swap_gbs,
-            # dominant kernel by time (ncu launch list: ~93% of the resolver step), bound by the host link
-            "roofline": {"bound": "host_link", "kernel": "swapin_kernel", "achieved": swap_gbs, "peak": h2d_peak,
-                         "unit": "GB/s", "frac": swap_gbs / h2d_peak,
+            # dominant kernel by time (ncu launch list: ~98% of the resolver step), bound by the host link
+            "roofline": {"bound": "host_link",
+                         "kernel": "swapin_bulk_kernel" if cfg.row <= 1024 else "swapin_kernel",
+                         "achieved": swap_gbs, "peak": h2d_peak, "unit": "GB/s", "frac": swap_gbs / h2d_peak,
                          "traffic": (SWAPIN_PCIE_READ_BYTES_PER_LAUNCH * installs / launches / SWAPIN_NCU_INSTALLS
-                                     if cfg.row == 656 else None),
+                                     if cfg.row == 656 and host.pitch == 768 else None),
                          "traffic_kind": "PCIe read bytes per launch (ncu pcie__read_bytes of the resolver "
                                          "workload, scaled to this run's installs per launch)",
                          "peak_source": "pinned cudaMemcpyAsync H2D 256 MiB, best of 10, this run"},
