@@ -38,3 +38,37 @@ def max_over_ranks(values: list[float], device: torch.device | str = "cpu") -> l
     if _initialized():
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     return t.tolist()
+
+
+def gpu_local_cpus(gpu_index: int, nvml=None) -> list[int]:
+    """Host CPUs that NVML reports as local to physical GPU ``gpu_index`` (its NUMA node's
+    cores), restricted to the CPUs this process may use; empty when NVML cannot tell."""
+    import os
+
+    try:
+        if nvml is None:
+            import pynvml as nvml
+        nvml.nvmlInit()
+        handle = nvml.nvmlDeviceGetHandleByIndex(gpu_index)
+        words = ((os.cpu_count() or 1) + 63) // 64
+        mask = nvml.nvmlDeviceGetCpuAffinity(handle, words)
+    except Exception:
+        return []
+    cpus = {w * 64 + b for w, word in enumerate(mask) for b in range(64) if (int(word) >> b) & 1}
+    return sorted(cpus & os.sched_getaffinity(0))
+
+
+def bind_to_gpu_local_cpus(gpu_index: int, nvml=None) -> list[int]:
+    """Run this process on the CPUs local to its GPU before it allocates the pinned host pool.
+
+    Page-locked host memory is placed on the NUMA node of the thread that allocates and first
+    touches it, and every swap-in reads that memory over the GPU's host link, so on a
+    multi-socket host the pool belongs on the GPU's socket.  Returns the CPUs bound (empty:
+    affinity left unchanged, e.g. a single-node host or no NVML)."""
+    import os
+
+    cpus = gpu_local_cpus(gpu_index, nvml)
+    if cpus and set(cpus) != os.sched_getaffinity(0):
+        os.sched_setaffinity(0, cpus)
+        return cpus
+    return []

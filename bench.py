@@ -299,6 +299,26 @@ def h2d_peak_gbs(torch, dev, d2h: bool = False) -> float:
     return best
 
 
+def h2d_peaks(torch, dev, world: int, rank: int) -> tuple[float, float]:
+    """(alone, concurrent) pinned H2D copy bandwidth of this rank's GPU: each rank in turn, then
+    all ranks at once.  With several GPUs the host side is shared, so a rank's swap-in is bounded
+    by the concurrent figure."""
+    if world == 1:
+        p = h2d_peak_gbs(torch, dev)
+        return p, p
+    import torch.distributed as dist
+
+    alone = 0.0
+    for r in range(world):
+        dist.barrier()
+        if r == rank:
+            alone = h2d_peak_gbs(torch, dev)
+    dist.barrier()
+    concurrent = h2d_peak_gbs(torch, dev)
+    dist.barrier()
+    return alone, concurrent
+
+
 class L2Flush:
     """Write 256 MiB (evicts everything), then read another 256 MiB so the write-back of dirty lines
     happens here, outside the timed region: the next step starts on a cold, clean L2."""
@@ -320,7 +340,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     import asu_ascend_b200
 
     asu_ascend_b200.load()
-    from asu_ascend_b200.dist import max_over_ranks, reduce_stats, shard_range
+    from asu_ascend_b200.dist import bind_to_gpu_local_cpus, max_over_ranks, reduce_stats, shard_range
     from asu_ascend_b200.host_pool import HostRowPool, check_status
     from asu_ascend_b200.lru import LruSlotPools
     from asu_ascend_b200.workloads import record_addresses_torch
@@ -341,6 +361,9 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
 
     # One pool per (layer, request), as the reference manager keeps one managed cache per layer
     # (patch/0003 asu_kv_cache_manager.py from_kv_caches, patch lines 339-403).
+    # the pinned pool goes on the NUMA node of this GPU's host CPUs (a no-op on single-node hosts)
+    all_cpus = os.sched_getaffinity(0)
+    bound_cpus = bind_to_gpu_local_cpus(gpu_index(local_rank))
     host = HostRowPool(POOL_ROWS if cfg.row <= 4096 else POOL_ROWS // 64, cfg.row, pitch=args.host_pitch or None)
     host.fill_random(11 + rank)
     recs = [record_addresses_torch(R, cfg.keys, host.rows, dev, key_offset=layer * cfg.keys,
@@ -350,7 +373,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     outs = [pools[0].new_output(), pools[0].new_output()]
     status = torch.zeros(R, dtype=torch.int32, device=dev)
     flush = L2Flush(torch, dev)
-    h2d_peak = h2d_peak_gbs(torch, dev)
+    h2d_alone, h2d_peak = h2d_peaks(torch, dev, world, rank)
 
     def total_stats():
         return sum(p.stats.sum(0) for p in pools)
@@ -434,7 +457,8 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
         swap_gbs = installs * cfg.row / (sum(swapin_ms) * 1e-3) / 1e9
         cpu = None
         if world == 1 and not args.no_cpu_baseline and cfg.name == "resolver":
-            threads = os.cpu_count() or 1
+            os.sched_setaffinity(0, all_cpus)  # the CPU leg uses every host thread again
+            threads = len(all_cpus)
             v, done, secs = cpu_port_run(cfg, R, trace, base, K_steps, args.cpu_sample_s, threads)
             cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
                    "sample": f"{done} steps x {R} requests x top-k {cfg.topk} ({secs:.1f} s, cycling the "
@@ -445,7 +469,8 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
                   "row_bytes": cfg.row,
                   "locality": (f"{int(cfg.reuse * 100)}% reuse + "
                                + (f"zipf({cfg.zipf})" if cfg.zipf else "uniform")),
-                  "host_pitch": host.pitch, "l2": L2_NOTE, "parallelism": f"request-sharded x{world}",
+                  "host_pitch": host.pitch, "host_cpus_bound": len(bound_cpus), "l2": L2_NOTE,
+                  "parallelism": f"request-sharded x{world}",
                   "prefill_steps": args.prefill}
         line = base_line(world, K_steps, W, max_ms / K_steps, idx_per_step * K_steps / (max_ms * 1e-3), config,
                          scaling="strong" if cfg.strong else "weak")
@@ -462,7 +487,9 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
                                      if cfg.row == 656 and host.pitch == 768 else None),
                          "traffic_kind": "PCIe read bytes per launch (ncu pcie__read_bytes of the resolver "
                                          "workload, scaled to this run's installs per launch)",
-                         "peak_source": "pinned cudaMemcpyAsync H2D 256 MiB, best of 10, this run"},
+                         "peak_source": ("pinned cudaMemcpyAsync H2D 256 MiB, best of 10, this run"
+                                         + ("" if world == 1 else ", all ranks copying at once")),
+                         "peak_alone": h2d_alone},
             "roofline_lru": {"bound": "hbm", "kernel": "lru_step_kernel", "achieved": achieved, "peak": hbm_peak,
                              "unit": "GB/s", "frac": achieved / hbm_peak,
                              "traffic": LRU_DRAM_BYTES_PER_LAUNCH if cfg.name == "resolver" else None,

@@ -70,3 +70,38 @@ def test_two_gloo_ranks_match_one_process(tmp_path):
     expect = _run_rows(_trace(6, 5), list(range(6))).sum(0)
     np.testing.assert_array_equal(got[:5], expect)
     assert got[5] == 2  # max over ranks of (rank + 1)
+
+
+class _FakeNvml:
+    """NVML stand-in: GPU i is local to CPUs [4i, 4i+4)."""
+
+    def nvmlInit(self):
+        pass
+
+    def nvmlDeviceGetHandleByIndex(self, i):
+        return i
+
+    def nvmlDeviceGetCpuAffinity(self, handle, words):
+        return [0xF << (4 * handle)] + [0] * (words - 1)
+
+
+def test_gpu_local_cpus_reads_nvml_affinity_within_the_allowed_set():
+    import os
+
+    from asu_ascend_b200.dist import bind_to_gpu_local_cpus, gpu_local_cpus
+
+    allowed = os.sched_getaffinity(0)
+    expect = sorted({4, 5, 6, 7} & allowed)
+    assert gpu_local_cpus(1, _FakeNvml()) == expect
+    try:
+        bound = bind_to_gpu_local_cpus(1, _FakeNvml())
+        if expect and set(expect) != allowed:
+            assert bound == expect and os.sched_getaffinity(0) == set(expect)
+    finally:
+        os.sched_setaffinity(0, allowed)
+
+    class Broken(_FakeNvml):
+        def nvmlInit(self):
+            raise RuntimeError("no driver")
+
+    assert gpu_local_cpus(0, Broken()) == [] and bind_to_gpu_local_cpus(0, Broken()) == []
