@@ -10,11 +10,12 @@
 //
 // B200 design: one CTA (1024 threads) per request row.
 //  * lookup: queries are processed in chunks of 2048 (two per thread, thread-contiguous).
-//    The first occurrence of each missing key is found with an atomicMin "claim" on the
-//    key's index entry (value INT32_MIN + position, so the lowest position wins), a
-//    block-wide exclusive scan over the first-occurrence flags gives each one its rank in
-//    query order, and rank k takes free_slots[head + k] -- the serial free_head++ order.
-//    Later duplicates read the installed slot after a barrier.
+//    While the query and index loads are in flight the CTA prefetches the free-list window
+//    free_slots[head .. head+2048) into shared memory.  The first occurrence of each missing
+//    key is found in a shared-memory hash (atomicMin of the position per key), a block-wide
+//    exclusive scan over the first-occurrence flags gives each one its rank in query order,
+//    and rank k takes free_slots[head + k] -- the serial free_head++ order.  Later
+//    duplicates read the allocated slot from the hash after a barrier.
 //  * maintain: the protected set is a shared-memory bitset; the ring is walked in
 //    thread-contiguous chunks, a scan over the evictable flags ranks candidates in ring
 //    order, and rank k < head is evicted into free_slots[head - 1 - k] -- the serial
@@ -29,6 +30,23 @@ constexpr int kThreads = 1024;
 constexpr int kItems = 2;                   // queries per thread per chunk
 constexpr int kChunk = kThreads * kItems;   // 2048 = the reference QUERY_COUNT
 
+constexpr int kHash = 2 * kChunk;           // shared-memory hash: at most kChunk keys, load <= 1/2
+
+// Claim `key` for chunk position `li` (the smallest position wins); returns the table index,
+// -1 only if the table were full, which kHash > kChunk rules out.
+__device__ __forceinline__ int claim_first(int32_t* keys, int32_t* first, int32_t key, int32_t li) {
+    uint32_t h = hash32(static_cast<uint32_t>(key)) & (kHash - 1);
+    for (int probe = 0; probe < kHash; ++probe) {
+        const int32_t prev = atomicCAS(keys + h, -1, key);
+        if (prev == -1 || prev == key) {
+            atomicMin(first + h, li);
+            return static_cast<int>(h);
+        }
+        h = (h + 1) & (kHash - 1);
+    }
+    return -1;
+}
+
 __global__ void __launch_bounds__(kThreads)
 ops_lookup_kernel(int32_t* __restrict__ index, int32_t* __restrict__ slot_to_index,
                   const int32_t* __restrict__ free_slots, int32_t* __restrict__ free_head,
@@ -36,6 +54,9 @@ ops_lookup_kernel(int32_t* __restrict__ index, int32_t* __restrict__ slot_to_ind
                   uint32_t index_size, uint32_t slot_count, uint32_t free_count, uint32_t query_count,
                   int32_t* status) {
     __shared__ int scan_buf[33];
+    __shared__ int32_t h_key[kHash];    // missing key; reused for its allocated slot after ranking
+    __shared__ int32_t h_first[kHash];  // first chunk position of the key
+    __shared__ int32_t s_free[kChunk];  // free_slots[head + k], prefetched
     for (uint32_t r = blockIdx.x; r < req_num; r += gridDim.x) {
         int32_t* irow = index + static_cast<uint64_t>(r) * index_size;
         int32_t* srow = slot_to_index + static_cast<uint64_t>(r) * slot_count;
@@ -45,6 +66,14 @@ ops_lookup_kernel(int32_t* __restrict__ index, int32_t* __restrict__ slot_to_ind
         int32_t head = ld_cg(free_head + r);
         int32_t bits = 0;
         for (uint32_t base = 0; base < query_count; base += kChunk) {
+            for (int i = threadIdx.x; i < kHash; i += kThreads) {
+                h_key[i] = -1;
+                h_first[i] = INT32_MAX;
+            }
+            for (int k = threadIdx.x; k < kChunk; k += kThreads) {
+                const int64_t f = static_cast<int64_t>(head) + k;
+                s_free[k] = (f >= 0 && f < static_cast<int64_t>(free_count)) ? __ldg(frow + f) : kNotFound;
+            }
             int32_t key[kItems], slot[kItems];
             bool miss[kItems];
 #pragma unroll
@@ -64,52 +93,57 @@ ops_lookup_kernel(int32_t* __restrict__ index, int32_t* __restrict__ slot_to_ind
                     }
                 }
             }
-            __syncthreads();  // every pre-chunk value is read before any claim lands
+            __syncthreads();  // tables cleared, free window loaded
+            int h[kItems];
 #pragma unroll
             for (int j = 0; j < kItems; ++j) {
-                if (miss[j])
-                    atomicMin(irow + key[j], kClaimBase + static_cast<int32_t>(threadIdx.x * kItems + j));
+                h[j] = miss[j] ? claim_first(h_key, h_first, key[j], static_cast<int32_t>(threadIdx.x * kItems + j)) : -1;
+                if (miss[j] && h[j] < 0) {
+                    bits |= ASU_ST_BAD_STATE;
+                    miss[j] = false;
+                }
             }
-            __syncthreads();
+            __syncthreads();  // every claim made
             int canon[kItems];
             int local = 0;
 #pragma unroll
             for (int j = 0; j < kItems; ++j) {
-                canon[j] = miss[j] && ld_cg(irow + key[j]) == kClaimBase + static_cast<int32_t>(threadIdx.x * kItems + j);
+                canon[j] = miss[j] && h_first[h[j]] == static_cast<int32_t>(threadIdx.x * kItems + j);
                 local += canon[j];
             }
             int total = 0;
-            int rank = block_exclusive_scan(local, scan_buf, &total);
+            int rank = block_exclusive_scan(local, scan_buf, &total);  // ends with a barrier: h_key is free
 #pragma unroll
             for (int j = 0; j < kItems; ++j) {
                 if (!canon[j]) continue;
-                const int64_t fidx = static_cast<int64_t>(head) + rank++;
+                const int32_t k = rank++;
                 int32_t s = kNotFound;
-                if (fidx >= 0 && fidx < static_cast<int64_t>(free_count)) {
-                    s = ld_cg(frow + fidx);
+                if (static_cast<int64_t>(head) + k < static_cast<int64_t>(free_count) && head + k >= 0) {
+                    s = s_free[k];
                 } else {
                     bits |= ASU_ST_FREE_EXHAUSTED;
                 }
-                st_cg(irow + key[j], s);
                 if (s >= 0 && static_cast<uint32_t>(s) < slot_count) {
+                    st_cg(irow + key[j], s);
                     st_cg(srow + s, key[j]);
                 } else if (s != kNotFound) {
+                    st_cg(irow + key[j], s);  // the reference stores whatever the free list holds
                     bits |= ASU_ST_BAD_STATE;
                 }
                 slot[j] = s;
-                miss[j] = false;
+                h_key[h[j]] = s;
             }
-            __syncthreads();
+            __syncthreads();  // allocated slots published
 #pragma unroll
             for (int j = 0; j < kItems; ++j) {
                 const uint32_t pos = base + threadIdx.x * kItems + j;
-                if (miss[j]) slot[j] = ld_cg(irow + key[j]);  // duplicate of an earlier miss
+                if (miss[j] && !canon[j]) slot[j] = h_key[h[j]];  // duplicate of an earlier miss
                 if (pos < query_count) orow[pos] = slot[j];
             }
             int64_t nh = static_cast<int64_t>(head) + total;
             if (nh > static_cast<int64_t>(free_count)) nh = free_count;
             head = static_cast<int32_t>(nh);
-            __syncthreads();
+            __syncthreads();  // before the next chunk clears the tables
         }
         if (threadIdx.x == 0) st_cg(free_head + r, head);
         if (bits) flag_status(status, r, bits);

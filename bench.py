@@ -24,6 +24,8 @@ Other workloads (`--workload`):
                 41,984-byte rows
   decode        1 request, 61 layers x npu_asu_resolve_kv_slots_single_req per decode step
   writeback     prefill write-back of a 128K-token context x 4 layers into the pinned pool
+  ops           asu_hbm_index_lookup / asu_hbm_index_maintain as the reference's op benchmark runs
+                them (req_num 1-8, hit/miss/mixed, state restored per call, 200 calls)
 All inputs are synthetic and seeded.
 
 Prints one JSON line (rank 0).  `value` is resolved indices/s for the whole job with inputs
@@ -105,7 +107,7 @@ def parse_args():
     p.add_argument("--prefill", type=int, default=8)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--workload", choices=("resolver", "lru1", "lookup", "multilayer", "stress", "stress-block", "decode",
-                            "writeback"),
+                            "writeback", "ops"),
                    default="resolver")
     p.add_argument("--seed", type=int, default=2026)
     p.add_argument("--cpu-sample-s", type=float, default=12.0)
@@ -425,6 +427,10 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     hit_host = torch.empty((R, cfg.topk), dtype=torch.bool, pin_memory=True)
     q_in = torch.empty((R, cfg.topk), dtype=torch.int32, device=dev)
     ev2 = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K_steps)]
+    # The slot ids and hit mask go back on a second stream while the swap-in reads host rows:
+    # the two copies run in opposite directions of the host link.
+    copy_stream = torch.cuda.Stream(dev)
+    main = torch.cuda.current_stream(dev)
     for k in range(K_steps):
         flush()
         torch.cuda._sleep(100_000)
@@ -433,9 +439,12 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             o = outs[(k * L + layer) % 2]
             q_in.copy_(q_host[base2 + k, layer], non_blocking=True)
             pools[layer].step(q_in, out=o)
+            copy_stream.wait_stream(main)
+            with torch.cuda.stream(copy_stream):
+                slot_host.copy_(o.slot, non_blocking=True)
+                hit_host.copy_(o.hit, non_blocking=True)
             host.swapin(recs[layer], q_in, o.slot, o.install, slot_pools[layer], status=status)
-            slot_host.copy_(o.slot, non_blocking=True)
-            hit_host.copy_(o.hit, non_blocking=True)
+            main.wait_stream(copy_stream)  # the outputs' buffer is reused two layers later
         ev2[k][1].record()
     torch.cuda.synchronize()
     e2e_ms = [e[0].elapsed_time(e[1]) for e in ev2]
@@ -953,6 +962,157 @@ def run_writeback(args, world: int, rank: int, local_rank: int):
     pool.close()
 
 
+# ------------------------------------------------------------------ ops lookup / maintain (reference harness)
+
+OPS_REQS = (1, 2, 4, 8)
+OPS_ITERS = 200
+
+
+def run_ops(args, world: int, rank: int, local_rank: int):
+    """asu_hbm_index_lookup and asu_hbm_index_maintain through the torch ops, timed the way the
+    reference's ops/scripts/bench_hbm_index_ops.py:100-140 times them: inputs from its case
+    builders (restated in workloads.py), state restored before every iteration outside the
+    timed region (plus an L2 flush), one op per timed interval, 200 iterations, p50.  Sweeps
+    req_num 1/2/4/8 x hit/miss/mixed for lookup and evict 25%/100% for maintain; the headline
+    is lookup, req_num 8, mixed."""
+    import torch
+
+    import asu_ascend_b200
+
+    asu_ascend_b200.load()
+    from asu_ascend_b200 import ops as _ops  # noqa: F401  (registers torch.ops.asu)
+    from asu_ascend_b200.dist import max_over_ranks
+    from asu_ascend_b200.workloads import QUERY_COUNT, make_index_case, make_maintain_case
+    from oracle import c_oracle
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    lookup, maintain = torch.ops.asu.asu_hbm_index_lookup, torch.ops.asu.asu_hbm_index_maintain
+    flush = L2Flush(torch, dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    iters = max(args.steps, OPS_ITERS)
+
+    def timed(restore, op):
+        ms = []
+        for i in range(args.warmup + iters):
+            restore()
+            flush()
+            torch.cuda._sleep(50_000)
+            a.record()
+            op()
+            b.record()
+            b.synchronize()
+            if i >= args.warmup:
+                ms.append(a.elapsed_time(b))
+        return ms
+
+    sweep, head = {}, None
+    for req in OPS_REQS:
+        for pattern in ("hit", "miss", "mixed"):
+            case = [torch.from_numpy(x).to(dev) for x in make_index_case(req, pattern)]
+            work = [x.clone() for x in case]
+
+            def restore(work=work, case=case):
+                for w_, c_ in zip(work[:4], case[:4]):
+                    w_.copy_(c_)
+
+            out = {}
+
+            def op(work=work, req=req, out=out):
+                out["slots"] = lookup(work[0], work[1], work[2], work[3], work[4], req)
+
+            ms = timed(restore, op)
+            sweep[f"lookup_req{req}_{pattern}_p50_us"] = statistics.median(ms) * 1e3
+            sweep[f"lookup_req{req}_{pattern}_mean_us"] = statistics.fmean(ms) * 1e3
+            if req == OPS_REQS[-1] and pattern == "mixed":
+                head = (case, ms, out["slots"], work)
+        for evict in (0.25, 1.0):
+            case = [torch.from_numpy(x).to(dev) for x in make_maintain_case(req, evict)]
+            work = [x.clone() for x in case]
+
+            def restore(work=work, case=case):
+                for w_, c_ in zip(work[:4], case[:4]):
+                    w_.copy_(c_)
+
+            def op(work=work, req=req):
+                maintain(work[0], work[1], work[2], work[3], work[4], req, args.seed)
+
+            ms = timed(restore, op)
+            sweep[f"maintain_req{req}_evict{int(evict * 100)}_p50_us"] = statistics.median(ms) * 1e3
+            sweep[f"maintain_req{req}_evict{int(evict * 100)}_mean_us"] = statistics.fmean(ms) * 1e3
+
+    case, ms, slots, work = head
+    R = OPS_REQS[-1]
+    # parity of the headline case against the C restatement of the reference lookup
+    np_case = [x.cpu().numpy() for x in case]
+    exp, exp_index, _, exp_head = c_oracle.ops_lookup(*np_case[:4], np_case[4])
+    if not (np.array_equal(slots.cpu().numpy(), exp) and np.array_equal(work[0].cpu().numpy(), exp_index)
+            and np.array_equal(work[3].cpu().numpy(), exp_head)):
+        raise RuntimeError("ops lookup differs from the oracle")
+    # e2e through the op: host query in, slot ids out
+    q_host = case[4].cpu().pin_memory()
+    out_host = torch.empty(q_host.shape, dtype=torch.int32, pin_memory=True)
+    q_dev = torch.empty_like(case[4])
+    e2e = []
+    for i in range(args.warmup + iters):
+        for w_, c_ in zip(work[:4], case[:4]):
+            w_.copy_(c_)
+        flush()
+        torch.cuda.synchronize()
+        a.record()
+        q_dev.copy_(q_host, non_blocking=True)
+        out_host.copy_(lookup(work[0], work[1], work[2], work[3], q_dev, R), non_blocking=True)
+        b.record()
+        b.synchronize()
+        if i >= args.warmup:
+            e2e.append(a.elapsed_time(b))
+    p50, p50_e2e = statistics.median(ms), statistics.median(e2e)
+    p50, p50_e2e = max_over_ranks([p50, p50_e2e], dev)
+    if rank != 0:
+        return
+    n = R * QUERY_COUNT
+    misses = int((exp_head - np_case[3]).sum())
+    alg = n * 13 + misses * 12
+    hbm = float(load_peaks().get("hbm_gbs", 6650.0))
+    achieved = alg / (p50 * 1e-3) / 1e9
+    # CPU leg: the C restatement, state copied outside the timer, ~3 s
+    cpu_n, cpu_s = 0, 0.0
+    if not args.no_cpu_baseline:
+        L = c_oracle.lib()
+        t_end = time.perf_counter() + 3.0
+        while time.perf_counter() < t_end:
+            idx, s2i, fs, fh, q = (np.ascontiguousarray(x.copy()) for x in np_case)
+            o = np.empty(q.shape, np.int32)
+            p_ = c_oracle._p
+            t0 = time.perf_counter()
+            L.ops_lookup(p_(idx), p_(s2i), p_(fs), p_(fh), p_(q), p_(o), R, idx.shape[1], s2i.shape[1], fs.shape[1],
+                         q.shape[1])
+            cpu_s += time.perf_counter() - t0
+            cpu_n += n
+    line = base_line(world, iters, args.warmup, p50, world * n / (p50 * 1e-3),
+                     {"workload": f"ops: asu_hbm_index_lookup, {R} requests x {QUERY_COUNT} queries, mixed pattern "
+                                  "(reference harness case: 8192 resident of a 131072-entry index, half the queries "
+                                  "miss and allocate), state restored before every timed call; sweep over req_num "
+                                  "1/2/4/8 x hit/miss/mixed and asu_hbm_index_maintain at 25%/100% eviction",
+                      "l2": "flushed after the state restore, before every timed call"})
+    line.update({"metric": "asu_hbm_index_lookup queries/sec (p50 of 200 restored calls)", "p50_lookup_us": p50 * 1e3,
+                 "timer_note": "CUDA event differences on this GPU come in steps of 1.024 us; the sweep also "
+                               "reports means",
+                 "sweep": sweep,
+                 "roofline": {"bound": "hbm", "kernel": "ops_lookup_kernel", "achieved": achieved, "peak": hbm,
+                              "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                              "algorithmic_bytes_per_launch": alg,
+                              "note": "13 B per query + 12 B per allocation; 8 requests are 8 CTAs: latency-bound"},
+                 "e2e": {"value": world * n / (p50_e2e * 1e-3), "unit": UNIT, "h2d_bytes_per_step": n * 4,
+                         "d2h_bytes_per_step": n * 4},
+                 "gpu_launches": iters,
+                 "cpu_baseline": None if not cpu_n else {
+                     "value": cpu_n / cpu_s, "unit": UNIT, "cores": 1, "kind": "port",
+                     "sample": "C restatement of the reference lookup on the same 8-request case, state restored "
+                               "between calls, ~3 s"}})
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -976,6 +1136,8 @@ def main():
             run_decode(args, world, rank, local_rank)
         elif args.workload == "writeback":
             run_writeback(args, world, rank, local_rank)
+        elif args.workload == "ops":
+            run_ops(args, world, rank, local_rank)
         else:
             run_lookup(args, world, rank, local_rank)
     finally:

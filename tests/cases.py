@@ -4,72 +4,17 @@ from __future__ import annotations
 
 import numpy as np
 
-INDEX_SIZE = 128 * 1024
-SLOT_COUNT = 10 * 1024
-RESIDENT_SLOT_COUNT = 8 * 1024
-FREE_SLOT_COUNT = 2 * 1024
-QUERY_COUNT = 2 * 1024
-NOT_FOUND = -1
-
-
-def make_query(pattern: str, req_id: int) -> np.ndarray:
-    """ops/scripts/asu_hbm_index_common.py:100-116 (the 'mixed' pattern plants duplicates at 1025, 1027)."""
-    hit_query = np.arange(QUERY_COUNT, dtype=np.int32) % RESIDENT_SLOT_COUNT
-    miss_base = 20_000 + req_id * 3_000
-    miss_query = ((miss_base + np.arange(QUERY_COUNT, dtype=np.int32)) % INDEX_SIZE).astype(np.int32)
-    if pattern == "hit":
-        return hit_query
-    if pattern == "miss":
-        return miss_query
-    if pattern == "mixed":
-        q = hit_query.copy()
-        q[QUERY_COUNT // 2:] = miss_query[: QUERY_COUNT // 2]
-        q[QUERY_COUNT // 2 + 1] = q[QUERY_COUNT // 2]
-        q[QUERY_COUNT // 2 + 3] = q[QUERY_COUNT // 2 + 2]
-        return q
-    raise ValueError(pattern)
-
-
-def make_index_case(req_num: int, pattern: str):
-    """ops/scripts/asu_hbm_index_common.py:80-97 -> (index, slot_to_index, free_slots, free_head, query)."""
-    index = np.full((req_num, INDEX_SIZE), NOT_FOUND, np.int32)
-    s2i = np.full((req_num, SLOT_COUNT), NOT_FOUND, np.int32)
-    free_slots = np.empty((req_num, FREE_SLOT_COUNT), np.int32)
-    free_head = np.zeros(req_num, np.int32)
-    query = np.empty((req_num, QUERY_COUNT), np.int32)
-    keys = np.arange(RESIDENT_SLOT_COUNT, dtype=np.int32)
-    for r in range(req_num):
-        index[r, keys] = keys
-        s2i[r, keys] = keys
-        free_slots[r] = np.arange(RESIDENT_SLOT_COUNT, SLOT_COUNT, dtype=np.int32)
-        query[r] = make_query(pattern, r)
-    return index, s2i, free_slots, free_head, query
-
-
-def make_maintain_case(req_num: int, evict_ratio: float):
-    """ops/scripts/asu_hbm_index_common.py:148-176 -> (index, s2i, free_slots, free_head, last_query_slots)."""
-    evict = int(round(FREE_SLOT_COUNT * evict_ratio))
-    index = np.full((req_num, INDEX_SIZE), NOT_FOUND, np.int32)
-    s2i = np.full((req_num, SLOT_COUNT), NOT_FOUND, np.int32)
-    free_slots = np.empty((req_num, FREE_SLOT_COUNT), np.int32)
-    free_head = np.full(req_num, evict, np.int32)
-    lq = np.empty((req_num, QUERY_COUNT), np.int32)
-    keys = np.arange(RESIDENT_SLOT_COUNT, dtype=np.int32)
-    miss_keys = 20_000 + np.arange(evict, dtype=np.int32)
-    alloc = RESIDENT_SLOT_COUNT + np.arange(evict, dtype=np.int32)
-    hit_count = QUERY_COUNT - evict
-    for r in range(req_num):
-        index[r, keys] = keys
-        s2i[r, keys] = keys
-        free_slots[r] = np.arange(RESIDENT_SLOT_COUNT, SLOT_COUNT, dtype=np.int32)
-        if evict:
-            index[r, miss_keys] = alloc
-            s2i[r, alloc] = miss_keys
-        if hit_count:
-            lq[r, :hit_count] = np.arange(hit_count, dtype=np.int32)
-        if evict:
-            lq[r, hit_count:] = alloc
-    return index, s2i, free_slots, free_head, lq
+from asu_ascend_b200.workloads import (  # noqa: F401  (restated reference harness cases)
+    FREE_SLOT_COUNT,
+    INDEX_SIZE,
+    NOT_FOUND,
+    QUERY_COUNT,
+    RESIDENT_SLOT_COUNT,
+    SLOT_COUNT,
+    make_index_case,
+    make_maintain_case,
+    make_query,
+)
 
 
 def apply_changes(base: np.ndarray, idx: np.ndarray, val: np.ndarray) -> np.ndarray:
