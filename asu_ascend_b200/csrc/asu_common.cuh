@@ -71,6 +71,35 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* 
     return res;
 }
 
+// Block-wide exclusive scan with a single __syncthreads(): every warp scans the per-warp
+// totals itself instead of waiting for one warp to do it.  `warp_sums` (32 ints of shared
+// memory) is read after the barrier, so the caller must not write it again before another
+// barrier -- alternate two buffers between back-to-back scans.  Returns the exclusive prefix
+// and writes the block total to *total; every thread of the block must call it.
+__device__ __forceinline__ int block_exclusive_scan_1b(int v, int* warp_sums, int* total) {
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int nwarps = blockDim.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, d);
+        if (lane >= d) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    const int w = lane < nwarps ? warp_sums[lane] : 0;
+    int s = w;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, s, d);
+        if (lane >= d) s += y;
+    }
+    const int before = __shfl_sync(0xffffffffu, s - w, warp);  // sum of the warps before this one
+    *total = __shfl_sync(0xffffffffu, s, 31);
+    return before + x - v;
+}
+
 }  // namespace asu
 
 // Host-side launch-error helper shared by the entry points.

@@ -62,7 +62,7 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
     int32_t* s_hpos = s_hkey + H;      // [H]  hash: first position
     int32_t* s_hval = s_hpos + H;      // [H]  hash: installed slot
     int32_t* s_stack = s_hval + H;     // [Q]  stack entries below the pushed victims, top first
-    __shared__ int scan_buf[33];
+    __shared__ int scan_a[32], scan_b[32];  // alternating buffers of the one-barrier block scans
     __shared__ int n_hits, n_valid;
     const int tid = threadIdx.x;
 
@@ -101,7 +101,11 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
             // inside the dynamic allocation, see lru_smem_bytes)
             const uint32_t S4 = (S + 3) / 4;
             for (uint32_t i = tid; i < S4; i += kThreads) reinterpret_cast<int4*>(s_last)[i] = m1;
-            for (uint32_t i = tid; i < H / 4; i += kThreads) reinterpret_cast<int4*>(s_hkey)[i] = m1;
+            const int4 big = make_int4(INT32_MAX, INT32_MAX, INT32_MAX, INT32_MAX);
+            for (uint32_t i = tid; i < H / 4; i += kThreads) {
+                reinterpret_cast<int4*>(s_hkey)[i] = m1;
+                reinterpret_cast<int4*>(s_hpos)[i] = big;
+            }
         }
         if (tid == 0) {
             n_hits = 0;
@@ -169,17 +173,13 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
                     h = (h + 1) & (H - 1);
                 }
                 hidx[j] = static_cast<int32_t>(h);
-                if (s_hkey[h] == key[j]) s_hpos[h] = 0x7fffffff;  // benign same-value race
+                atomicMin(&s_hpos[h], pos);  // the first position of the key wins
             } else {
                 st[j] = kBad;
                 bits |= ASU_ST_BAD_STATE;
             }
         }
-        __syncthreads();
-#pragma unroll
-        for (int j = 0; j < IPT_Q; ++j)
-            if (st[j] == kMiss) atomicMin(&s_hpos[hidx[j]], static_cast<int32_t>(tid * IPT_Q + j));
-        __syncthreads();
+        __syncthreads();  // every claim made
 
         // ---- P3: first occurrences pop the stack in query order ----
         int canon[IPT_Q];
@@ -190,7 +190,7 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
             local += canon[j];
         }
         int n_canon = 0;
-        int rank = block_exclusive_scan(local, scan_buf, &n_canon);
+        int rank = block_exclusive_scan_1b(local, scan_a, &n_canon);
         int32_t slot[IPT_Q];
         uint8_t inst[IPT_Q];
 #pragma unroll
@@ -281,8 +281,6 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
             if (live && static_cast<uint32_t>(oldv[j]) >= S) bits |= ASU_ST_BAD_STATE;
             keep_local += keep[j];
         }
-        int n_keep = 0;
-        int a = block_exclusive_scan(keep_local, scan_buf, &n_keep);
         bool touched[IPT_Q];
         int touched_local = 0;
 #pragma unroll
@@ -290,8 +288,14 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
             touched[j] = slot[j] >= 0 && s_last[slot[j]] == static_cast<int32_t>(tid * IPT_Q + j);
             touched_local += touched[j];
         }
-        int n_touched = 0;
-        int b = block_exclusive_scan(touched_local, scan_buf, &n_touched);  // its barriers end all s_order reads
+        // one scan for both counts: kept residents in the low 16 bits (<= S <= 16384), touched
+        // slots in the high bits (<= Q <= 4096); its barrier ends all reads of the old order
+        int packed_total = 0;
+        const int packed = block_exclusive_scan_1b(keep_local | (touched_local << 16), scan_b, &packed_total);
+        int a = packed & 0xffff;
+        int b = packed >> 16;
+        const int n_keep = packed_total & 0xffff;
+        const int n_touched = packed_total >> 16;
         // A consistent state has n_keep + n_touched == S - free2 <= S; the guards only matter
         // for corrupt input (duplicate slots across the maps), which is flagged below.
 #pragma unroll

@@ -485,6 +485,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
                          scaling="strong" if cfg.strong else "weak")
         line.update({
             "p50_resolve_us": statistics.median(resolve_ms) * 1e3,
+            "mean_resolve_us": statistics.fmean(resolve_ms) * 1e3,
             "p50_swapin_us": statistics.median(swapin_ms) * 1e3,
             "miss_rate": installs / (launches * R * cfg.topk),
             "swapin_gbs": swap_gbs,
@@ -566,7 +567,8 @@ def run_lru1(args, world: int, rank: int, local_rank: int):
                          world * 2048 * args.steps / (tot_ms * 1e-3),
                          {"workload": "lru1: 1 request/GPU, 131072 keys, 16384 slots, LRU target 2048, top-k 2048 "
                                       "(70% reuse + zipf 1.1), maintain + lookup only", "l2": L2_NOTE})
-        line.update({"p50_resolve_us": statistics.median(ms) * 1e3, "gpu_launches": args.steps,
+        line.update({"p50_resolve_us": statistics.median(ms) * 1e3, "mean_resolve_us": statistics.fmean(ms) * 1e3,
+                     "gpu_launches": args.steps,
                      "cpu_baseline": {"value": 2048 * args.steps / cpu_s, "unit": UNIT, "cores": 1, "kind": "port",
                                       "sample": f"the same {args.steps} steps, C restatement, one thread"},
                      "e2e": None})
