@@ -5,19 +5,25 @@ Each operator is defined twice with the same schema: under ``torch.ops.asu`` and
 (ascend-ops/torch_binding_asu_hbm_index.cpp:7-25; patch/0001 csrc/torch_binding.cpp hunk,
 patch lines 810-826), so code written against the reference resolves to these CUDA
 implementations unchanged.  The CUDA implementations call libasu_b200.so through its C
-ABI on the current stream; there is no CPU implementation (a CPU tensor raises).
+ABI on the current stream; there is no CPU implementation (a CPU tensor raises).  The
+lookup / maintain / batch-LRU ops are registered here in Python; the single-request
+resolver, which a decode step calls once per layer, is registered in C++ by
+libasu_torch.so (csrc/torch_binding.cpp), which this module loads.
 
 Host-side argument checks mirror the reference adapters' TORCH_CHECKs
 (ascend-ops/asu_hbm_index_lookup/asu_hbm_index_lookup_torch_adpt.h:22-27,
 asu_hbm_index_maintain_torch_adpt.h:22-27) plus device / contiguity / shape checks that
 the raw pointers need.  Device-side problems are written to a status word; with
-``set_status_checks(True)`` every op synchronises and raises AsuError on a non-zero
-status (off by default: the ops stay asynchronous like the NPU ones).
+``set_status_checks(True)`` every op synchronises and raises on a non-zero status
+(AsuError from the Python ops, RuntimeError from the C++ resolver op; AsuError is a
+RuntimeError) -- off by default: the ops stay asynchronous like the NPU ones.
 """
 
 from __future__ import annotations
 
+import ctypes
 import os
+from pathlib import Path
 
 import torch
 from torch.library import Library
@@ -31,10 +37,29 @@ _STATUS_CHECKS = os.environ.get("ASU_CHECK_STATUS", "0") not in ("", "0")
 _IGNORED_STATUS = _lib.ST_SHORTAGE  # counted in the stats, not an error
 
 
+TORCH_LIB_PATH = Path(__file__).resolve().with_name("libasu_torch.so")
+
+
+def _load_torch_binding() -> ctypes.CDLL:
+    """Register npu_asu_resolve_kv_slots_single_req from the C++ binding (csrc/torch_binding.cpp)."""
+    if not TORCH_LIB_PATH.exists():
+        raise ImportError(f"{TORCH_LIB_PATH} is not built: run `python -m asu_ascend_b200.build`; "
+                          "asu_ascend_b200 has no CPU fallback")
+    torch.ops.load_library(str(TORCH_LIB_PATH))
+    handle = ctypes.CDLL(str(TORCH_LIB_PATH))  # the same loaded image: shares the status-check flag
+    handle.asu_torch_set_status_checks.argtypes = [ctypes.c_int]
+    handle.asu_torch_set_status_checks.restype = None
+    return handle
+
+
+_torch_binding = _load_torch_binding()
+
+
 def set_status_checks(enabled: bool) -> None:
     """Synchronise after every op and raise on a device status (debug / tests)."""
     global _STATUS_CHECKS
     _STATUS_CHECKS = bool(enabled)
+    _torch_binding.asu_torch_set_status_checks(int(_STATUS_CHECKS))
 
 
 def status_checks_enabled() -> bool:
@@ -141,79 +166,6 @@ def asu_hbm_index_lookup_simt(token_to_slot, slot_to_token, lru_slots, query_tok
     return slot_ids, miss_mask
 
 
-_KV_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
-
-
-def _as_i32_input(name: str, t: torch.Tensor, dev) -> torch.Tensor:
-    """Read-only index inputs: int64 is narrowed to int32 (the NPU op takes int32 only)."""
-    if t.device != dev:
-        raise RuntimeError(f"{name} must be on {dev}")
-    if t.dtype == torch.int64:
-        t = t.to(torch.int32)
-    if t.dtype != torch.int32:
-        raise RuntimeError(f"{name} must be int32")
-    return t.contiguous()
-
-
-def npu_asu_resolve_kv_slots_single_req(original_topk_indices, actual_seq_len, managed_prefix_len, token_state,
-                                        asu_record_addr, hbm_slot_of_token, slot_owner_token, free_slot_stack,
-                                        free_slot_count, original_block_table, original_kv_cache_0,
-                                        original_kv_cache_1, managed_kv_cache_0, managed_kv_cache_1, block_size):
-    """Single-request resolver; returns resolved_kv_slots (int32, topk's shape)."""
-    del managed_prefix_len  # unused by the reference as well (patch line 970)
-    if actual_seq_len < 0:
-        raise ValueError("actual_seq_len must be non-negative")
-    if block_size <= 0:
-        raise ValueError("block_size must be positive")
-    dev = token_state.device
-    for n, t in (("token_state", token_state), ("hbm_slot_of_token", hbm_slot_of_token),
-                 ("slot_owner_token", slot_owner_token), ("free_slot_count", free_slot_count)):
-        _req_cuda_i32(n, t, dev)
-    topk = _as_i32_input("original_topk_indices", original_topk_indices, dev)
-    record = _as_i32_input("asu_record_addr", asu_record_addr, dev)
-    stack = _as_i32_input("free_slot_stack", free_slot_stack, dev)
-    block_table = _as_i32_input("original_block_table", original_block_table, dev)
-    o0, o1, m0, m1 = original_kv_cache_0, original_kv_cache_1, managed_kv_cache_0, managed_kv_cache_1
-    for n, t in (("original_kv_cache_0", o0), ("original_kv_cache_1", o1), ("managed_kv_cache_0", m0),
-                 ("managed_kv_cache_1", m1)):
-        if t.dim() < 1:
-            raise ValueError(f"{n} must have a slot dimension")
-        if t.device != dev or not t.is_contiguous():
-            raise RuntimeError(f"{n} must be a contiguous tensor on {dev}")
-        if t.dtype not in _KV_DTYPES:
-            raise RuntimeError(f"{n} must be float16, bfloat16 or float32")
-    if o0.shape[1:] != m0.shape[1:]:
-        raise ValueError("original_kv_cache_0 and managed_kv_cache_0 must have matching per-slot shapes")
-    if o1.shape[1:] != m1.shape[1:]:
-        raise ValueError("original_kv_cache_1 and managed_kv_cache_1 must have matching per-slot shapes")
-    if o0.dtype != m0.dtype or o1.dtype != m1.dtype:
-        raise RuntimeError("original and managed KV caches must have the same dtype")
-    n = topk.numel()
-    resolved = torch.empty(original_topk_indices.shape, dtype=torch.int32, device=dev)
-    if n == 0:
-        return resolved
-    rb0 = (o0.numel() // max(o0.shape[0], 1)) * o0.element_size()
-    rb1 = (o1.numel() // max(o1.shape[0], 1)) * o1.element_size()
-    src_rows = min(o0.shape[0], o1.shape[0])
-    slot_count = min(m0.shape[0], m1.shape[0], slot_owner_token.numel())
-    max_seq = min(token_state.numel(), hbm_slot_of_token.numel(), record.numel())
-    ws = torch.empty(int(lib.asu_kv_resolver_workspace_bytes(n)), dtype=torch.uint8, device=dev)
-    # the status word is only read when status checks are on; without them the kernel gets no
-    # status pointer and the call launches exactly the resolver's two kernels
-    status = _new_status(1, dev) if _STATUS_CHECKS else None
-    with torch.cuda.device(dev):
-        check(lib.asu_kv_resolver_do(
-            _stream(token_state), topk.data_ptr(), n, token_state.data_ptr(), record.data_ptr(),
-            hbm_slot_of_token.data_ptr(), slot_owner_token.data_ptr(), stack.data_ptr(), free_slot_count.data_ptr(),
-            stack.numel(), block_table.data_ptr(), block_table.numel(), o0.data_ptr(), o1.data_ptr(),
-            m0.data_ptr(), m1.data_ptr(), rb0, rb1, src_rows, slot_count, max_seq, actual_seq_len, block_size,
-            resolved.data_ptr(), ws.data_ptr(), None if status is None else status.data_ptr()),
-            "npu_asu_resolve_kv_slots_single_req")
-    if status is not None:
-        _raise_on_status(status, "npu_asu_resolve_kv_slots_single_req", ignore=0)
-    return resolved
-
-
 # ------------------------------------------------------------------ registration
 
 _SCHEMAS = {
@@ -224,18 +176,11 @@ _SCHEMAS = {
                                "int seed) -> ()"),
     "asu_hbm_index_lookup_simt": ("asu_hbm_index_lookup_simt(Tensor(a!) token_to_slot, Tensor(b!) slot_to_token, "
                                   "Tensor(c!) lru_slots, Tensor query_token_ids, int req_num) -> (Tensor, Tensor)"),
-    "npu_asu_resolve_kv_slots_single_req": (
-        "npu_asu_resolve_kv_slots_single_req(Tensor original_topk_indices, int actual_seq_len, "
-        "int managed_prefix_len, Tensor! token_state, Tensor asu_record_addr, Tensor! hbm_slot_of_token, "
-        "Tensor! slot_owner_token, Tensor free_slot_stack, Tensor! free_slot_count, Tensor original_block_table, "
-        "Tensor original_kv_cache_0, Tensor original_kv_cache_1, Tensor! managed_kv_cache_0, "
-        "Tensor! managed_kv_cache_1, int block_size) -> Tensor"),
 }
 _IMPLS = {
     "asu_hbm_index_lookup": asu_hbm_index_lookup,
     "asu_hbm_index_maintain": asu_hbm_index_maintain,
     "asu_hbm_index_lookup_simt": asu_hbm_index_lookup_simt,
-    "npu_asu_resolve_kv_slots_single_req": npu_asu_resolve_kv_slots_single_req,
 }
 
 
@@ -252,16 +197,10 @@ def _meta_simt(token_to_slot, slot_to_token, lru_slots, query_token_ids, req_num
                                                           device=query_token_ids.device)
 
 
-def _meta_resolve(original_topk_indices, *args):
-    # patch/0001 csrc/torch_binding_meta.cpp hunk (patch lines 592-625)
-    return torch.empty(original_topk_indices.shape, dtype=torch.int32, device=original_topk_indices.device)
-
-
 _METAS = {
     "asu_hbm_index_lookup": _meta_lookup,
     "asu_hbm_index_maintain": _meta_maintain,
     "asu_hbm_index_lookup_simt": _meta_simt,
-    "npu_asu_resolve_kv_slots_single_req": _meta_resolve,
 }
 
 _LIBRARIES: list[Library] = []
@@ -280,3 +219,4 @@ def _register() -> None:
 
 
 _register()
+set_status_checks(_STATUS_CHECKS)

@@ -106,8 +106,32 @@ def test_ops_reject_cpu_tensors_and_bad_arguments():
         ops.asu_hbm_index_lookup(z, z, z, z, z, 0)
     with pytest.raises(RuntimeError, match="int32"):
         ops.asu_hbm_index_maintain(z.float(), z, z, z, z, 1, 0)
+    f = torch.ops.asu.npu_asu_resolve_kv_slots_single_req  # C++ op: argument checks on host tensors too
+    kv = torch.zeros(4, 2)
     with pytest.raises(ValueError, match="block_size"):
-        ops.npu_asu_resolve_kv_slots_single_req(z, 4, 4, z, z, z, z, z, z, z, z, z, z, z, 0)
+        f(z, 4, 4, z, z, z, z, z, z, z, kv, kv, kv, kv, 0)
+    with pytest.raises(ValueError, match="actual_seq_len"):
+        f(z, -1, 4, z, z, z, z, z, z, z, kv, kv, kv, kv, 2)
+    with pytest.raises(RuntimeError, match="CUDA tensor"):
+        f(z, 4, 4, z, z, z, z, z, z, z, kv, kv, kv, kv, 2)
+    with pytest.raises(RuntimeError, match="int32"):
+        f(z, 4, 4, z.float(), z, z, z, z, z, z, kv, kv, kv, kv, 2)
+
+
+def test_torch_binding_formats_numbers_and_links_the_process_libstdcxx():
+    """libasu_torch.so must use the process's libstdc++ (a second, statically linked copy
+    crashes on the first formatted number); its host-memory refusal formats an integer."""
+    import subprocess
+
+    from asu_ascend_b200 import ops
+
+    z = torch.zeros(7, dtype=torch.int32)
+    kv = torch.zeros(4, 2)
+    with pytest.raises(RuntimeError, match="got 7 elements in host memory"):
+        torch.ops.asu.npu_asu_resolve_kv_slots_single_req(z, 7, 7, z, z, z, z, z, z, z, kv, kv, kv, kv, 2)
+    out = subprocess.run(["nm", "-D", "--defined-only", str(ops.TORCH_LIB_PATH)], capture_output=True, text=True)
+    if out.returncode == 0:
+        assert "codecvt" not in out.stdout and "_txnal_cow_string" not in out.stdout
 
 
 def test_meta_kernels_give_output_shapes():
