@@ -245,8 +245,13 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
                 install_mask[o] = inst[j];
             }
         }
-        if (hits_local) atomicAdd(&n_hits, hits_local);
-        if (valid_local) atomicAdd(&n_valid, valid_local);
+        // one shared-memory atomic per warp, not per thread (1024 adds to one address serialise)
+        hits_local = __reduce_add_sync(0xffffffffu, hits_local);
+        valid_local = __reduce_add_sync(0xffffffffu, valid_local);
+        if ((tid & 31) == 0) {
+            if (hits_local) atomicAdd(&n_hits, hits_local);
+            if (valid_local) atomicAdd(&n_valid, valid_local);
+        }
         __syncthreads();
 
         // ---- P5: new LRU order ----
