@@ -192,7 +192,8 @@ int asu_swapin_gather(void* stream, const void* host_pool, int64_t pool_rows, ui
 
 /* Producer side of the swap-in: host_pool[dst_row ? dst_row[i] : i] = src[src_index ? src_index[i]
  * : i] for i < n (rows of row_bytes; src rows src_pitch bytes apart in device memory, host rows
- * host_pitch bytes apart, 0 = row_bytes); dst_row[i] < 0 skips item i.  Replaces the MicroKV
+ * host_pitch bytes apart, 0 = row_bytes); dst_row[i] < 0 skips item i.  A host row's padding
+ * (host_pitch - row_bytes) under 128 bytes is written with zeros too.  Replaces the MicroKV
  * batch_put of prefilled records (docs/v0.1/kv-cache-offload-v0.1-real-ops-design.md:243-292;
  * MicroKV/python/microkv/client.py batch_put).  Out-of-range rows set ASU_ST_BAD_STATE (host
  * row) or ASU_ST_BAD_SOURCE (source row) in status[0] (nullable) and are skipped.  row_bytes and

@@ -1,6 +1,8 @@
 """Host-pool producer on the GPU: the write-back kernel's bytes, and the producer -> swap-in
 round trip (rows written back by the GPU come back into the HBM slot pool unchanged)."""
 
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -14,7 +16,8 @@ def test_writeback_rows_and_skips():
     from asu_ascend_b200.host_pool import HostRowPool
 
     pool = HostRowPool(rows=5000, row_bytes=656)
-    pool.array[:] = 7
+    full = np.frombuffer((ctypes.c_uint8 * pool.nbytes).from_address(pool._host), np.uint8).reshape(5000, pool.pitch)
+    full[:] = 7  # rows and their padding
     g = torch.Generator(device=DEV).manual_seed(2)
     src = torch.randint(0, 256, (3000, 656), dtype=torch.uint8, device=DEV, generator=g)
     dst = torch.randperm(5000, device=DEV, generator=g)[:3000].to(torch.int32)
@@ -28,6 +31,9 @@ def test_writeback_rows_and_skips():
     np.testing.assert_array_equal(pool.array[d[keep]], s[keep])
     untouched = np.setdiff1d(np.arange(5000), d[keep])
     assert (pool.array[untouched] == 7).all()
+    # a written row's padding up to the 768-byte pitch is zeroed (rows go out as whole lines);
+    # the other rows' padding is untouched
+    assert pool.pitch == 768 and (full[d[keep], 656:] == 0).all() and (full[untouched, 656:] == 7).all()
     # gathered sources and out-of-range rows
     idx = torch.tensor([5, 2999, 0, 3000, 1], dtype=torch.int32, device=DEV)
     rows = torch.tensor([10, 11, 5000, 12, -1], dtype=torch.int32, device=DEV)
