@@ -462,6 +462,44 @@ def test_swapin_bytes_exact(row_bytes, R, S, Q):
     pool.close()
 
 
+@pytest.mark.parametrize("row_bytes,pitch", [(656, None), (656, 656), (64, None), (1024, None), (2048, None)])
+def test_swapin_direct_masks_errors_and_pitches(row_bytes, pitch):
+    """The swap-in alone, on hand-made install masks: query counts that are not multiples of
+    32, installs into arbitrary slots, both kernels (bulk copies up to 1 KiB rows, 16-byte
+    loads above), packed and padded host rows, and out-of-range keys / slots / record rows,
+    which are skipped and reported while every valid row lands byte-exact."""
+    from asu_ascend_b200._lib import ST_BAD_QUERY, ST_BAD_SOURCE, ST_BAD_STATE
+    from asu_ascend_b200.host_pool import HostRowPool
+
+    rng = np.random.Generator(np.random.PCG64(row_bytes + (pitch or 0)))
+    R, Q, S, K = 3, 100, 300, 500
+    pool = HostRowPool(rows=700, row_bytes=row_bytes, pitch=pitch)
+    pool.fill_random(9)
+    rec = rng.integers(0, 700, (R, K)).astype(np.int32)
+    query = rng.integers(0, K, (R, Q)).astype(np.int32)
+    slot = np.stack([rng.permutation(S)[:Q] for _ in range(R)]).astype(np.int32)
+    install = rng.random((R, Q)) < 0.4
+    # planted errors (on installing positions only)
+    install[0, 5] = install[1, 7] = install[2, 9] = True
+    query[0, 5] = K + 3        # bad key
+    slot[1, 7] = S + 1         # bad slot
+    rec[2, query[2, 9]] = 700  # bad record row
+    ok = install.copy()
+    ok[0, 5] = ok[1, 7] = ok[2, 9] = False
+    # a valid install elsewhere must not share the bad record's key
+    same = (query[2] == query[2, 9]) & ok[2]
+    ok[2, same] = False
+    install[2, same] = False
+    base = rng.integers(0, 256, (R, S, row_bytes), dtype=np.uint8)
+    slot_pool = T(base)
+    status = torch.zeros(R, dtype=torch.int32, device=DEV)
+    pool.swapin(T(rec), T(query), T(slot), T(install), slot_pool, status=status)
+    expect = O.swapin(pool.array, np.minimum(rec, 699), query, slot, ok, base)
+    np.testing.assert_array_equal(N(slot_pool), expect)
+    assert N(status).tolist() == [ST_BAD_QUERY, ST_BAD_STATE, ST_BAD_SOURCE]
+    pool.close()
+
+
 # ------------------------------------------------------------------ resolver
 
 def test_resolver_reference_unit_vectors():
