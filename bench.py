@@ -264,15 +264,15 @@ def run_reference(args, world: int, rank: int):
     """Rank 0 times the CPU restatement on the default workload's config; other ranks exit."""
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0)) or 1
     cfg = RESOLVER_WORKLOADS["resolver"]
     base = args.prefill + args.warmup
     trace = make_trace(cfg, cfg.req, args.seed, base + args.steps)
     value, done, secs = cpu_port_run(cfg, cfg.req, trace, base, args.steps, args.cpu_sample_s, threads)
-    line = base_line(world, done, args.warmup, secs / done * 1e3, value,
+    line = base_line(world, args.steps, args.warmup, secs / done * 1e3, value,
                      {"workload": cfg.describe(), "requests_per_gpu": cfg.req, "topk": cfg.topk,
                       "context": cfg.keys, "slots_per_request": cfg.slots, "row_bytes": cfg.row})
-    line.update({"impl": "reference",
+    line.update({"impl": "reference", "cpu_steps_timed": done,
                  "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                                   "sample": f"{done} steps x {cfg.req} requests x top-k {cfg.topk} ({secs:.1f} s, "
                                             f"cycling the {args.steps} timed top-k sets after {base} untimed steps), "
