@@ -19,11 +19,12 @@
 //  * Eviction needs no sort: the victims are the head of the order row.  They are marked
 //    in shared memory (last_pos = -2), so a query that read a victim's slot before the
 //    eviction landed is classified as a miss -- exactly what the serial order (evict,
-//    then resolve) gives.  Victim unmapping stores happen while the gathers are in flight.
+//    then resolve) gives.  The victims' keys are loaded while the table gathers are in flight
+//    and unmapped after the classification (one barrier before any install).
 //  * The first occurrence of each missing key is found in a shared-memory hash table
 //    (atomicMin of the position per key); a block scan ranks first occurrences in query
 //    order and rank k pops the free stack: the victims just pushed (top first), then the
-//    older entries, which were prefetched into shared memory.  Later duplicates read the
+//    older entries, read on demand (none at the steady state).  Later duplicates read the
 //    installed slot from the hash entry (serially they are hits).
 //  * Every touch records its position in last_pos[slot] (shared-memory atomicMax); the
 //    new order is [untouched residents in old order] ++ [touched slots by last touching
@@ -61,7 +62,6 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
     int32_t* s_hkey = s_last + Sp;      // [H]  hash: key
     int32_t* s_hpos = s_hkey + H;      // [H]  hash: first position
     int32_t* s_hval = s_hpos + H;      // [H]  hash: installed slot
-    int32_t* s_stack = s_hval + H;     // [Q]  stack entries below the pushed victims, top first
     __shared__ int scan_a[32], scan_b[32];  // alternating buffers of the one-barrier block scans
     __shared__ int n_hits, n_valid;
     const int tid = threadIdx.x;
@@ -78,9 +78,18 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
         const int32_t free0 = ld_cg(count + r);
         const bool vec_row = (S % 4 == 0) && (reinterpret_cast<uintptr_t>(orow) % 16 == 0);
         if (vec_row) {
+            // all of a thread's row loads in flight before the first shared-memory store
+            // (S <= IPT_S * kThreads, so IPT_S / 4 16-byte loads per thread cover the row)
+            constexpr int kVec = (IPT_S + 3) / 4;
             const int4* src = reinterpret_cast<const int4*>(orow);
             int4* dst = reinterpret_cast<int4*>(s_order);
-            for (uint32_t i = tid; i < S / 4; i += kThreads) dst[i] = __ldcg(src + i);
+            int4 ov[kVec];
+#pragma unroll
+            for (int j = 0; j < kVec; ++j)
+                if (tid + j * kThreads < S / 4) ov[j] = __ldcg(src + tid + j * kThreads);
+#pragma unroll
+            for (int j = 0; j < kVec; ++j)
+                if (tid + j * kThreads < S / 4) dst[tid + j * kThreads] = ov[j];
         } else {
             for (uint32_t i = tid; i < S; i += kThreads) s_order[i] = ld_cg(orow + i);
         }
@@ -121,29 +130,49 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
         int32_t E = 0;
         if (free0 < tgt) E = (tgt - free0) < resident0 ? (tgt - free0) : resident0;
         const int32_t free1 = free0 + E;
-        // prefetch the free-stack entries the pops may reach below the pushed victims
-        const int32_t below = free0 < static_cast<int32_t>(Q) ? free0 : static_cast<int32_t>(Q);
-        for (int32_t i = tid; i < below; i += kThreads) s_stack[i] = ld_cg(krow + (free0 - 1 - i));
         __syncthreads();
 
-        // ---- P1: eviction of lru_order[0, E) ----
-        for (int32_t k = tid; k < E; k += kThreads) {
-            const int32_t v = s_order[k];
-            int32_t vkey = kNotFound;
-            if (static_cast<uint32_t>(v) < S) {
-                s_last[v] = kVictim;
-                vkey = ld_cg(srow + v);
-                if (static_cast<uint32_t>(vkey) < K) st_cg(trow + vkey, kNotFound);
-                else bits |= ASU_ST_BAD_STATE;
-                st_cg(srow + v, kNotFound);
-                st_cg(krow + free0 + k, v);
-            } else {
-                bits |= ASU_ST_BAD_STATE;
+        // ---- P1: eviction of lru_order[0, E): mark the victims now, load their keys; the
+        // unmapping stores follow the classification, so the loads overlap it ----
+        // (with more than 8 slots per thread the keys would not stay in registers: those
+        // configurations unmap the victims right here instead)
+        constexpr bool kDeferUnmap = IPT_S <= 8;
+        constexpr int kVict = kDeferUnmap ? IPT_S : 1;
+        int32_t vslot[kVict], vkey[kVict];
+        if constexpr (kDeferUnmap) {
+#pragma unroll
+            for (int i = 0; i < IPT_S; ++i) {
+                const int32_t k = tid + i * kThreads;
+                vslot[i] = k < E ? s_order[k] : kNotFound;
+                vkey[i] = kNotFound;
+                if (k < E) {
+                    if (static_cast<uint32_t>(vslot[i]) < S) {
+                        s_last[vslot[i]] = kVictim;
+                        vkey[i] = ld_cg(srow + vslot[i]);
+                    } else {
+                        bits |= ASU_ST_BAD_STATE;
+                    }
+                }
             }
-            if (static_cast<uint32_t>(k) < ev_stride) evicted[static_cast<uint64_t>(r) * ev_stride + k] = vkey;
+        } else {
+            for (int32_t k = tid; k < E; k += kThreads) {
+                const int32_t v = s_order[k];
+                int32_t vk = kNotFound;
+                if (static_cast<uint32_t>(v) < S) {
+                    s_last[v] = kVictim;
+                    vk = ld_cg(srow + v);
+                    if (static_cast<uint32_t>(vk) < K) st_cg(trow + vk, kNotFound);
+                    else bits |= ASU_ST_BAD_STATE;
+                    st_cg(srow + v, kNotFound);
+                    st_cg(krow + free0 + k, v);
+                } else {
+                    bits |= ASU_ST_BAD_STATE;
+                }
+                if (static_cast<uint32_t>(k) < ev_stride) evicted[static_cast<uint64_t>(r) * ev_stride + k] = vk;
+            }
         }
         if (tid == 0) ev_count[r] = E;
-        __syncthreads();  // victim marks visible; victim unmapping ordered before any install
+        __syncthreads();  // victim marks visible
 
         // ---- P2: classify; hits record their position, misses enter the hash ----
         uint8_t st[IPT_Q];
@@ -179,7 +208,21 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
                 bits |= ASU_ST_BAD_STATE;
             }
         }
-        __syncthreads();  // every claim made
+        // victim unmapping (P1's stores), ordered before any install by the barrier below
+#pragma unroll
+        for (int i = 0; i < (kDeferUnmap ? IPT_S : 0); ++i) {
+            const int32_t k = tid + i * kThreads;
+            if (k >= E) continue;
+            const int32_t v = vslot[i];
+            if (static_cast<uint32_t>(v) < S) {
+                if (static_cast<uint32_t>(vkey[i]) < K) st_cg(trow + vkey[i], kNotFound);
+                else bits |= ASU_ST_BAD_STATE;
+                st_cg(srow + v, kNotFound);
+                st_cg(krow + free0 + k, v);
+            }
+            if (static_cast<uint32_t>(k) < ev_stride) evicted[static_cast<uint64_t>(r) * ev_stride + k] = vkey[i];
+        }
+        __syncthreads();  // every claim made; victims unmapped
 
         // ---- P3: first occurrences pop the stack in query order ----
         int canon[IPT_Q];
@@ -202,7 +245,9 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
             const int32_t k = rank++;
             int32_t s = kNotFound;
             if (k < free1) {
-                s = k < E ? s_order[E - 1 - k] : s_stack[k - E];
+                // the victims just pushed (top first), then the older entries below them,
+                // read on demand: at the steady state every pop takes a victim
+                s = k < E ? s_order[E - 1 - k] : ld_cg(krow + (free0 - 1 - (k - E)));
                 if (static_cast<uint32_t>(s) >= S) {
                     bits |= ASU_ST_BAD_STATE;
                     s = kNotFound;
@@ -330,13 +375,14 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
         if (tid == 0) {
             st_cg(count + r, free2);
             if (n_keep + n_touched != static_cast<int>(S) - free2) bits |= ASU_ST_BAD_STATE;
-            if (stats != nullptr) {
-                int64_t* row = stats + static_cast<uint64_t>(r) * ASU_LRU_STAT_COLS;
-                row[ASU_LRU_STAT_HITS] += n_hits;
-                row[ASU_LRU_STAT_MISSES] += n_valid - n_hits;
-                row[ASU_LRU_STAT_INSTALLS] += n_inst;
-                row[ASU_LRU_STAT_SHORTAGES] += n_valid - n_hits - n_inst;
-                row[ASU_LRU_STAT_EVICTIONS] += E;
+            if (stats != nullptr) {  // reductions without a return value: nothing to wait for
+                unsigned long long* row =
+                    reinterpret_cast<unsigned long long*>(stats + static_cast<uint64_t>(r) * ASU_LRU_STAT_COLS);
+                atomicAdd(row + ASU_LRU_STAT_HITS, static_cast<unsigned long long>(n_hits));
+                atomicAdd(row + ASU_LRU_STAT_MISSES, static_cast<unsigned long long>(n_valid - n_hits));
+                atomicAdd(row + ASU_LRU_STAT_INSTALLS, static_cast<unsigned long long>(n_inst));
+                atomicAdd(row + ASU_LRU_STAT_SHORTAGES, static_cast<unsigned long long>(n_valid - n_hits - n_inst));
+                atomicAdd(row + ASU_LRU_STAT_EVICTIONS, static_cast<unsigned long long>(E));
             }
         }
         if (bits) flag_status(status, r, bits);
@@ -350,14 +396,14 @@ inline uint32_t pow2ceil(uint32_t x) {
     return p;
 }
 
-// Dynamic shared memory of one launch: order + last_pos rows, the hash table, the stack prefetch.
+// Dynamic shared memory of one launch: order + last_pos rows and the hash table.
 inline size_t lru_smem_bytes(uint32_t S, uint32_t Q, int* log2h_out) {
     const uint64_t Sp = (S + 3) & ~3u;
     uint32_t h = 2 * pow2ceil(Q < 16 ? 16 : Q);
-    size_t bytes = (2ull * Sp + 3ull * h + Q) * sizeof(int32_t);
+    size_t bytes = (2ull * Sp + 3ull * h) * sizeof(int32_t);
     if (bytes > 200u * 1024u) {  // large S and Q together: load factor up to 1 (still terminates)
         h /= 2;
-        bytes = (2ull * Sp + 3ull * h + Q) * sizeof(int32_t);
+        bytes = (2ull * Sp + 3ull * h) * sizeof(int32_t);
     }
     int l = 0;
     while ((1u << l) < h) ++l;
