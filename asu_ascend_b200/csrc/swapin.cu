@@ -283,3 +283,15 @@ extern "C" int asu_host_pool_free(void* host_ptr) {
     cudaError_t e = cudaFreeHost(host_ptr);
     return e == cudaSuccess ? ASU_OK : ASU_ERR_CUDA_BASE + static_cast<int>(e);
 }
+
+extern "C" int asu_host_device_pointer(const void* host_ptr, void** device_ptr) {
+    if (!host_ptr || !device_ptr) return ASU_ERR_ARG;
+    void* d = nullptr;
+    const cudaError_t e = cudaHostGetDevicePointer(&d, const_cast<void*>(host_ptr), 0);
+    if (e != cudaSuccess) {
+        cudaGetLastError();  // not page-locked and mapped: leave no error behind
+        return ASU_ERR_CUDA_BASE + static_cast<int>(e);
+    }
+    *device_ptr = d;
+    return ASU_OK;
+}

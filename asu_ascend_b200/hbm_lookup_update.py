@@ -11,6 +11,8 @@ lookup-only benchmark: any table width, plus the hit mask (entry != not_found).
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from ._lib import check, lib
@@ -100,18 +102,50 @@ def update_only(table_keys, table_states, query_keys, new_states, seed, update_p
               "hbm_random_update_do")
 
 
+def _kernel_ptr(t: torch.Tensor, name: str, dtype: torch.dtype, dev: torch.device) -> int:
+    """Address a kernel on ``dev`` can use for ``t``: a CUDA tensor on ``dev``, or pinned host
+    memory, which the kernel reads / writes over the host link directly (no staging copy)."""
+    if t.dtype != dtype:
+        raise RuntimeError(f"{name} must be {dtype}")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+    if t.device.type == "cuda":
+        if t.device != dev:
+            raise RuntimeError(f"{name} must be on {dev}")
+        return t.data_ptr()
+    if not t.is_pinned():
+        raise RuntimeError(f"{name} must be a CUDA tensor or pinned host memory")
+    d = ctypes.c_void_p()
+    check(lib.asu_host_device_pointer(t.data_ptr(), ctypes.byref(d)), f"{name}: device address of pinned memory")
+    return d.value
+
+
 def lookup(table: torch.Tensor, query: torch.Tensor, not_found: int = -1, status: torch.Tensor | None = None,
            out: torch.Tensor | None = None, hit: torch.Tensor | None = None):
-    """Gather ``table[r, query[r, i]]`` for a [R, T] table and [R, Q] queries; returns (out, hit_mask)."""
+    """Gather ``table[r, query[r, i]]`` for a [R, T] table and [R, Q] queries; returns (out, hit_mask).
+
+    ``table`` lives in HBM.  ``query``, ``out`` and ``hit`` may be CUDA tensors or pinned host
+    tensors: the kernel then reads the queries from, and writes the results to, host memory
+    itself (zero-copy; synchronise the stream before reading host results).  Outputs default to
+    the query's placement."""
     _check_i32(table, "table")
-    _check_i32(query, "query")
+    dev = table.device
     if table.dim() != 2 or query.dim() != 2 or table.shape[0] != query.shape[0]:
         raise RuntimeError("table must be [R, T] and query [R, Q]")
     R, Q = query.shape
-    out = torch.empty_like(query) if out is None else out
-    hit = torch.empty(query.shape, dtype=torch.bool, device=query.device) if hit is None else hit
-    with torch.cuda.device(query.device):
-        check(lib.asu_gather_lookup(torch.cuda.current_stream(query.device).cuda_stream, table.data_ptr(),
-                                    table.shape[1], query.data_ptr(), Q, out.data_ptr(), Q, hit.data_ptr(), R,
+    on_host = query.device.type == "cpu"
+    if out is None:
+        out = torch.empty(query.shape, dtype=torch.int32, pin_memory=True) if on_host else torch.empty_like(query)
+    if hit is None:
+        hit = (torch.empty(query.shape, dtype=torch.bool, pin_memory=True) if on_host
+               else torch.empty(query.shape, dtype=torch.bool, device=dev))
+    if out.shape != query.shape or hit.shape != query.shape:
+        raise RuntimeError("out and hit must have the query's shape")
+    qp = _kernel_ptr(query, "query", torch.int32, dev)
+    op = _kernel_ptr(out, "out", torch.int32, dev)
+    hp = _kernel_ptr(hit, "hit", torch.bool, dev)
+    with torch.cuda.device(dev):
+        check(lib.asu_gather_lookup(torch.cuda.current_stream(dev).cuda_stream, table.data_ptr(),
+                                    table.shape[1], qp, Q, op, Q, hp, R,
                                     not_found, None if status is None else status.data_ptr()), "asu_gather_lookup")
     return out, hit

@@ -207,6 +207,11 @@ int asu_host_pool_writeback(void* stream, void* host_pool, int64_t pool_rows, ui
 int asu_host_pool_alloc(uint64_t bytes, void** host_ptr, void** device_ptr);
 int asu_host_pool_free(void* host_ptr);
 
+/* Device address of page-locked, mapped host memory (any pinned allocation, e.g. a torch pinned
+ * tensor); fails for memory the GPU cannot address, so a kernel is never handed such a pointer.
+ * Used to let kernels read their inputs from and write their outputs to host buffers directly. */
+int asu_host_device_pointer(const void* host_ptr, void** device_ptr);
+
 /* ======================================================================
  * single-request KV resolver (patch 0001 asu_kv_resolver custom op)
  * ==================================================================== */

@@ -105,6 +105,28 @@ def test_lookup_only_workload_full_size():
     assert 0.8 < exp_hit.mean() < 0.9
 
 
+def test_lookup_zero_copy_host_buffers():
+    """Queries read from, results written to pinned host memory by the kernel itself."""
+    from asu_ascend_b200 import hbm_lookup_update as H
+    from asu_ascend_b200.workloads import lookup_only_case
+
+    table, query = lookup_only_case(req_num=8)
+    q_host = torch.from_numpy(query).pin_memory()
+    out, hit = H.lookup(T(table), q_host)
+    torch.cuda.synchronize()
+    assert out.device.type == "cpu" and out.is_pinned() and hit.is_pinned()
+    exp, exp_hit = O.gather_lookup(table, query)
+    np.testing.assert_array_equal(out.numpy(), exp)
+    np.testing.assert_array_equal(hit.numpy(), exp_hit)
+    # mixed placement: device queries, host results
+    out2 = torch.full(query.shape, 7, dtype=torch.int32).pin_memory()
+    H.lookup(T(table), T(query), out=out2)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out2.numpy(), exp)
+    with pytest.raises(RuntimeError, match="pinned"):
+        H.lookup(T(table), torch.from_numpy(query))  # pageable host memory is refused
+
+
 def test_gather_out_of_range_keys_flag_status():
     from asu_ascend_b200 import hbm_lookup_update as H
 
