@@ -300,3 +300,32 @@ def make_maintain_case(req_num: int, evict_ratio: float):
         if evict:
             lq[r, hit_count:] = alloc
     return index, s2i, free_slots, free_head, lq
+
+
+# ------------------------------------------------------------------ batch-LRU (SIMT) cases
+# Restated from pta-ops/asu_hbm_index_lookup_simt/python/random_workload.py: every slot
+# resident (token t in slot t, LRU order = slot order), and per request a unique 2K query with
+# exactly `hit_count` resident tokens and the rest drawn from the non-resident range, shuffled.
+# The random draws are this project's own (numpy), so the queries differ from the reference's.
+
+SIMT_SLOT_COUNT = 10 * 1024
+
+
+def simt_case(req_num: int, hit_count: int, seed: int = 0):
+    """(token_to_slot [R, 128K] int32, slot_to_token [R, 10K] int32, lru_slots [R, 10K] int16,
+    query [R, 2K] int32)."""
+    if not 0 <= hit_count <= QUERY_COUNT:
+        raise ValueError(f"hit_count must be in [0, {QUERY_COUNT}]")
+    rng = np.random.Generator(np.random.PCG64(seed))
+    t2s = np.full((req_num, INDEX_SIZE), NOT_FOUND, np.int32)
+    t2s[:, :SIMT_SLOT_COUNT] = np.arange(SIMT_SLOT_COUNT, dtype=np.int32)
+    s2t = np.tile(np.arange(SIMT_SLOT_COUNT, dtype=np.int32), (req_num, 1))
+    lru = np.tile(np.arange(SIMT_SLOT_COUNT, dtype=np.int16), (req_num, 1))
+    query = np.empty((req_num, QUERY_COUNT), np.int32)
+    for r in range(req_num):
+        hits = rng.choice(SIMT_SLOT_COUNT, hit_count, replace=False)
+        misses = SIMT_SLOT_COUNT + rng.choice(INDEX_SIZE - SIMT_SLOT_COUNT, QUERY_COUNT - hit_count, replace=False)
+        q = np.concatenate([hits, misses]).astype(np.int32)
+        rng.shuffle(q)
+        query[r] = q
+    return t2s, s2t, lru, query

@@ -25,7 +25,8 @@ Other workloads (`--workload`):
   decode        1 request, 61 layers x npu_asu_resolve_kv_slots_single_req per decode step
   writeback     prefill write-back of a 128K-token context x 4 layers into the pinned pool
   ops           asu_hbm_index_lookup / asu_hbm_index_maintain as the reference's op benchmark runs
-                them (req_num 1-8, hit/miss/mixed, state restored per call, 200 calls)
+                them (req_num 1-8, hit/miss/mixed, state restored per call, 200 calls), plus the
+                batch-LRU SIMT op and the gather + random update
 All inputs are synthetic and seeded.
 
 Prints one JSON line (rank 0).  `value` is resolved indices/s for the whole job with inputs
@@ -1046,6 +1047,41 @@ def run_ops(args, world: int, rank: int, local_rank: int):
             sweep[f"maintain_req{req}_evict{int(evict * 100)}_p50_us"] = statistics.median(ms) * 1e3
             sweep[f"maintain_req{req}_evict{int(evict * 100)}_mean_us"] = statistics.fmean(ms) * 1e3
 
+    # batch-LRU (SIMT contract) on the reference's random cases, and the gather + 5% random update
+    from asu_ascend_b200 import hbm_lookup_update as H
+    from asu_ascend_b200.workloads import lookup_only_case, simt_case
+
+    simt = torch.ops.asu.asu_hbm_index_lookup_simt
+    for req in (1, 8, 64):
+        for hits in (1536, 2048):
+            case_s = [torch.from_numpy(x).to(dev) for x in simt_case(req, hits, seed=req)]
+            work_s = [x.clone() for x in case_s]
+
+            def restore(work=work_s, case=case_s):
+                for w_, c_ in zip(work[:3], case[:3]):
+                    w_.copy_(c_)
+
+            def op(work=work_s, req=req):
+                simt(work[0], work[1], work[2], work[3], req)
+
+            ms_s = timed(restore, op)
+            sweep[f"simt_req{req}_hit{hits}_p50_us"] = statistics.median(ms_s) * 1e3
+            sweep[f"simt_req{req}_hit{hits}_mean_us"] = statistics.fmean(ms_s) * 1e3
+    table_u, query_u = lookup_only_case()
+    tk = torch.from_numpy(table_u).to(dev)
+    ts0 = torch.from_numpy(table_u).to(dev)
+    ts = ts0.clone()
+    tq = torch.from_numpy(query_u).to(dev)
+    tn = torch.randint(0, 1 << 20, tq.shape, dtype=torch.int32, device=dev)
+
+    def restore_u():
+        ts.copy_(ts0)
+
+    ms_u = timed(restore_u, lambda: H.lookup_random_update(tk, ts, tq, tn, seed=args.seed, update_percent=5))
+    sweep["lookup_random_update_64x2048_p5_p50_us"] = statistics.median(ms_u) * 1e3
+    ms_u = timed(restore_u, lambda: H.update_only(tk, ts, tq, tn, seed=args.seed, update_percent=5))
+    sweep["update_only_64x2048_p5_p50_us"] = statistics.median(ms_u) * 1e3
+
     case, ms, slots, work = head
     R = OPS_REQS[-1]
     # parity of the headline case against the C restatement of the reference lookup
@@ -1098,7 +1134,9 @@ def run_ops(args, world: int, rank: int, local_rank: int):
                      {"workload": f"ops: asu_hbm_index_lookup, {R} requests x {QUERY_COUNT} queries, mixed pattern "
                                   "(reference harness case: 8192 resident of a 131072-entry index, half the queries "
                                   "miss and allocate), state restored before every timed call; sweep over req_num "
-                                  "1/2/4/8 x hit/miss/mixed and asu_hbm_index_maintain at 25%/100% eviction",
+                                  "1/2/4/8 x hit/miss/mixed, asu_hbm_index_maintain at 25%/100% eviction, "
+                                  "asu_hbm_index_lookup_simt (req 1/8/64, 1536/2048 hits of 2048) and the "
+                                  "gather + 5% random update on 64 x 128K tables",
                       "l2": "flushed after the state restore, before every timed call"})
     line.update({"metric": "asu_hbm_index_lookup queries/sec (p50 of 200 restored calls)", "p50_lookup_us": p50 * 1e3,
                  "timer_note": "CUDA event differences on this GPU come in steps of 1.024 us; the sweep also "
