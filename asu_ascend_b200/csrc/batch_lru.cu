@@ -8,12 +8,16 @@
 //   miss i     takes evictable[i]; its old token is unmapped; maps are rebound
 //   new lru    = evictable[M:] + evictable[:M] + hit slots
 //
-// B200 design: one CTA (1024 threads) per request; all scratch in shared memory (hit flags,
-// victim list), so the caller's workspace is not needed.  First occurrences are found with
-// the atomicMin claim used by the other lookups (the reference kernel's CAS winner is
-// scheduling-dependent; the oracle's is the first occurrence, which is what this returns).
-// The stable partition of the LRU row is one block scan over packed (hit, evictable)
-// counts with the row held in registers, so the row is rewritten in place.
+// B200 design: one CTA (1024 threads) per request; all scratch in shared memory, so the
+// caller's workspace is not needed.  At launch every thread issues its loads together: the
+// query gathers from token_to_slot, its part of the LRU row (kept in registers) and the
+// slot_to_token row (into shared memory, where the victims' old tokens are read later).
+// First occurrences of missing tokens are claimed in a shared-memory hash (the reference
+// kernel's CAS winner is scheduling-dependent; the oracle's is the first occurrence, which is
+// what this returns); a block scan ranks them in query order.  The stable partition of the
+// LRU row is one block scan over packed (hit, evictable) counts, and the row is rewritten in
+// place.  Later duplicates read their first occurrence's slot from the hash, so no output
+// needs a second global read.
 #include "asu_common.cuh"
 
 namespace asu {
@@ -22,15 +26,40 @@ namespace {
 constexpr int kThreads = 1024;
 enum : uint8_t { kInvalid = 0, kHit = 1, kMiss = 2 };
 
+__device__ __forceinline__ int batch_claim(int32_t* keys, int32_t* first, uint32_t H, int32_t key, int32_t pos) {
+    uint32_t h = hash32(static_cast<uint32_t>(key)) & (H - 1);
+    for (uint32_t probe = 0; probe < H; ++probe) {
+        const int32_t prev = atomicCAS(keys + h, -1, key);
+        if (prev == -1 || prev == key) {
+            atomicMin(first + h, pos);
+            return static_cast<int>(h);
+        }
+        h = (h + 1) & (H - 1);
+    }
+    return -1;  // unreachable: H >= 2 * Q
+}
+
+// Dynamic shared memory: slot_to_token row [Sp], hash keys / first position / slot [3H],
+// victim list [Q], hit flags [S] bytes.
+inline size_t batch_smem_bytes(uint32_t S, uint32_t Q, uint32_t H) {
+    const size_t Sp = (S + 3) & ~3u;
+    return (Sp + 3ull * H + Q) * sizeof(int32_t) + S;
+}
+
 template <int IPT_Q, int IPT_S>
 __global__ void __launch_bounds__(kThreads)
 batch_lru_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int16_t* __restrict__ lru,
                  const int32_t* __restrict__ query, int32_t* __restrict__ slot_ids, uint8_t* __restrict__ miss_mask,
-                 uint32_t req_num, uint32_t K, uint32_t S, uint32_t Q, int32_t* status) {
+                 uint32_t req_num, uint32_t K, uint32_t S, uint32_t Q, uint32_t H, int32_t* status) {
     extern __shared__ int32_t dyn[];
-    int32_t* vict = dyn;                                        // [Q]
-    uint8_t* hitf = reinterpret_cast<uint8_t*>(dyn + Q);        // [S]
-    __shared__ int scan_buf[33];
+    const uint32_t Sp = (S + 3) & ~3u;
+    int32_t* s_owner = dyn;                                     // [Sp] slot_to_token row
+    int32_t* h_key = s_owner + Sp;                              // [H]
+    int32_t* h_first = h_key + H;                               // [H]
+    int32_t* h_slot = h_first + H;                              // [H] slot given to the key
+    int32_t* vict = h_slot + H;                                 // [Q]
+    uint8_t* hitf = reinterpret_cast<uint8_t*>(vict + Q);       // [S]
+    __shared__ int scan_a[32], scan_b[32];
     const int tid = threadIdx.x;
     for (uint32_t r = blockIdx.x; r < req_num; r += gridDim.x) {
         int32_t* trow = t2s + static_cast<uint64_t>(r) * K;
@@ -38,83 +67,114 @@ batch_lru_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int16_t* 
         int16_t* lrow = lru + static_cast<uint64_t>(r) * S;
         const int32_t* qrow = query + static_cast<uint64_t>(r) * Q;
         int32_t bits = 0;
-        for (uint32_t s = tid; s < S; s += kThreads) hitf[s] = 0;
-        __syncthreads();
 
-        int32_t key[IPT_Q], slot[IPT_Q];
-        uint8_t st[IPT_Q];
+        // ---- loads: queries -> token_to_slot gathers, LRU row, slot_to_token row ----
+        int32_t key[IPT_Q], g[IPT_Q];
 #pragma unroll
         for (int j = 0; j < IPT_Q; ++j) {
             const uint32_t pos = tid * IPT_Q + j;
-            key[j] = -1;
-            slot[j] = kNotFound;
-            st[j] = kInvalid;
-            if (pos < Q) {
-                key[j] = __ldg(qrow + pos);
-                if (static_cast<uint32_t>(key[j]) < K) {
-                    const int32_t v = ld_cg(trow + key[j]);
-                    if (v >= 0 && static_cast<uint32_t>(v) < S) {
-                        st[j] = kHit;
-                        slot[j] = v;
-                        hitf[v] = 1;
-                    } else if (v == kNotFound) {
-                        st[j] = kMiss;
-                    } else {
-                        bits |= ASU_ST_BAD_STATE;  // the oracle raises on these
-                    }
+            key[j] = pos < Q ? __ldg(qrow + pos) : -1;
+            g[j] = kNotFound;
+            if (pos < Q && static_cast<uint32_t>(key[j]) < K) g[j] = ld_cg(trow + key[j]);
+        }
+        int32_t lv[IPT_S];
+        bool vec_lru = false;
+        if constexpr (IPT_S % 8 == 0) vec_lru = S % 8 == 0 && (reinterpret_cast<uintptr_t>(lrow) & 15) == 0;
+        if constexpr (IPT_S % 8 == 0) {
+          if (vec_lru) {
+            // 16-byte loads of 8 int16 entries each
+#pragma unroll
+            for (int j = 0; j < IPT_S; j += 8) {
+                const uint32_t idx = tid * IPT_S + j;
+                if (idx < S) {
+                    const int4 v4 = __ldcg(reinterpret_cast<const int4*>(lrow + idx));
+                    const int16_t* e = reinterpret_cast<const int16_t*>(&v4);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) lv[j + u] = e[u];
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) lv[j + u] = -1;
                 }
             }
+          }
         }
-        __syncthreads();
+        if (!vec_lru) {
 #pragma unroll
-        for (int j = 0; j < IPT_Q; ++j)
-            if (st[j] == kMiss) atomicMin(trow + key[j], kClaimBase + static_cast<int32_t>(tid * IPT_Q + j));
-        __syncthreads();
+            for (int j = 0; j < IPT_S; ++j) {
+                const uint32_t idx = tid * IPT_S + j;
+                lv[j] = idx < S ? static_cast<int32_t>(lrow[idx]) : -1;
+            }
+        }
+        for (uint32_t i = tid; i < S; i += kThreads) s_owner[i] = ld_cg(srow + i);
+        for (uint32_t i = tid; i < H; i += kThreads) {
+            h_key[i] = -1;
+            h_first[i] = INT32_MAX;
+        }
+        for (uint32_t i = tid; i < S; i += kThreads) hitf[i] = 0;
+        __syncthreads();  // tables cleared, slot_to_token row in shared memory
+
+        // ---- classify: hits flag their slot, missing tokens claim their first position ----
+        int32_t slot[IPT_Q], h[IPT_Q];
+        uint8_t st[IPT_Q];
+#pragma unroll
+        for (int j = 0; j < IPT_Q; ++j) {
+            const int32_t pos = static_cast<int32_t>(tid * IPT_Q + j);
+            slot[j] = kNotFound;
+            h[j] = -1;
+            st[j] = kInvalid;
+            if (static_cast<uint32_t>(pos) >= Q || static_cast<uint32_t>(key[j]) >= K) continue;
+            const int32_t v = g[j];
+            if (v >= 0 && static_cast<uint32_t>(v) < S) {
+                st[j] = kHit;
+                slot[j] = v;
+                hitf[v] = 1;
+            } else if (v == kNotFound) {
+                h[j] = batch_claim(h_key, h_first, H, key[j], pos);
+                if (h[j] >= 0) st[j] = kMiss;
+                else bits |= ASU_ST_BAD_STATE;
+            } else {
+                bits |= ASU_ST_BAD_STATE;  // the oracle raises on these
+            }
+        }
+        __syncthreads();  // claims and hit flags complete
         int canon[IPT_Q];
         int local = 0;
 #pragma unroll
         for (int j = 0; j < IPT_Q; ++j) {
-            canon[j] = st[j] == kMiss && ld_cg(trow + key[j]) == kClaimBase + static_cast<int32_t>(tid * IPT_Q + j);
+            canon[j] = st[j] == kMiss && h_first[h[j]] == static_cast<int32_t>(tid * IPT_Q + j);
             local += canon[j];
         }
         int M = 0;
-        int mrank = block_exclusive_scan(local, scan_buf, &M);
+        int mrank = block_exclusive_scan_1b(local, scan_a, &M);
 
-        // stable partition of the LRU row (held in registers)
-        int32_t lv[IPT_S];
+        // ---- stable partition of the LRU row (held in registers) ----
         bool lh[IPT_S];
         int packed = 0;
 #pragma unroll
         for (int j = 0; j < IPT_S; ++j) {
             const uint32_t idx = tid * IPT_S + j;
-            lv[j] = -1;
             lh[j] = false;
-            if (idx < S) {
-                lv[j] = lrow[idx];
-                if (static_cast<uint32_t>(lv[j]) < S) {
-                    lh[j] = hitf[lv[j]] != 0;
-                    packed += lh[j] ? (1 << 16) : 1;
-                } else {
-                    bits |= ASU_ST_BAD_STATE;
-                }
+            if (idx >= S) continue;
+            if (static_cast<uint32_t>(lv[j]) < S) {
+                lh[j] = hitf[lv[j]] != 0;
+                packed += lh[j] ? (1 << 16) : 1;
+            } else {
+                bits |= ASU_ST_BAD_STATE;
             }
         }
         int ptotal = 0;
-        int pre = block_exclusive_scan(packed, scan_buf, &ptotal);
+        const int pre = block_exclusive_scan_1b(packed, scan_b, &ptotal);
         const int V = ptotal & 0xffff;
         int hrank = pre >> 16, erank = pre & 0xffff;
 #pragma unroll
         for (int j = 0; j < IPT_S; ++j) {
-            if (lv[j] < 0 || static_cast<uint32_t>(lv[j]) >= S || lh[j]) continue;
+            if (static_cast<uint32_t>(lv[j]) >= S || lh[j]) continue;
             if (erank < M) vict[erank] = lv[j];
             ++erank;
         }
-        __syncthreads();
+        __syncthreads();  // victim list complete
 
-        if (M > V) {  // block-uniform: not enough evictable slots; undo the claims, change nothing
-#pragma unroll
-            for (int j = 0; j < IPT_Q; ++j)
-                if (canon[j]) st_cg(trow + key[j], kNotFound);
+        if (M > V) {  // block-uniform: not enough evictable slots; nothing was written, change nothing
             if (tid == 0) bits |= ASU_ST_NO_VICTIM;
 #pragma unroll
             for (int j = 0; j < IPT_Q; ++j) {
@@ -129,19 +189,21 @@ batch_lru_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int16_t* 
             for (int j = 0; j < IPT_Q; ++j) {
                 if (!canon[j]) continue;
                 const int32_t victim = vict[mrank++];
-                const int32_t vt = ld_cg(srow + victim);
+                const int32_t vt = s_owner[victim];
                 if (vt >= 0) {
                     if (static_cast<uint32_t>(vt) < K) st_cg(trow + vt, kNotFound);
                     else bits |= ASU_ST_BAD_STATE;
                 }
                 st_cg(srow + victim, key[j]);
                 st_cg(trow + key[j], victim);
+                slot[j] = victim;
+                h_slot[h[j]] = victim;
             }
             // new order: stale evictables, then this batch's victims, then hit slots
             erank = pre & 0xffff;
 #pragma unroll
             for (int j = 0; j < IPT_S; ++j) {
-                if (lv[j] < 0 || static_cast<uint32_t>(lv[j]) >= S) continue;
+                if (static_cast<uint32_t>(lv[j]) >= S) continue;
                 int dst;
                 if (lh[j]) {
                     dst = V + hrank++;
@@ -151,14 +213,13 @@ batch_lru_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int16_t* 
                 }
                 lrow[dst] = static_cast<int16_t>(lv[j]);
             }
-            __syncthreads();
+            __syncthreads();  // first occurrences' slots published
 #pragma unroll
             for (int j = 0; j < IPT_Q; ++j) {
                 const uint32_t pos = tid * IPT_Q + j;
                 if (pos >= Q) continue;
-                int32_t out = kNotFound;
-                if (static_cast<uint32_t>(key[j]) < K) out = ld_cg(trow + key[j]);
-                slot_ids[static_cast<uint64_t>(r) * Q + pos] = out;
+                if (st[j] == kMiss && !canon[j]) slot[j] = h_slot[h[j]];  // later duplicate of a miss
+                slot_ids[static_cast<uint64_t>(r) * Q + pos] = slot[j];
                 miss_mask[static_cast<uint64_t>(r) * Q + pos] = canon[j] ? 1 : 0;
             }
         }
@@ -171,21 +232,36 @@ template <int IPT_Q, int IPT_S>
 int launch_batch(cudaStream_t s, int32_t* t2s, int32_t* s2t, int16_t* lru, const int32_t* q, int32_t* slot_ids,
                  uint8_t* mask, uint32_t R, uint32_t K, uint32_t S, uint32_t Q, int32_t* status) {
     static unsigned long long configured = 0;  // one bit per device
+    static int max_dynamic[64];
     int dev = 0;
-    cudaGetDevice(&dev);
-    const int max_smem = kThreads * IPT_Q * 4 + kThreads * IPT_S;
-    if (dev < 64 && !((configured >> dev) & 1ull)) {
-        cudaError_t e = cudaFuncSetAttribute(batch_lru_kernel<IPT_Q, IPT_S>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return e != cudaSuccess ? ASU_ERR_CUDA_BASE + static_cast<int>(e) : ASU_ERR_ARG;
+    }
+    if (!((configured >> dev) & 1ull)) {
+        int optin = 0;
+        cudaFuncAttributes fa;
+        e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, batch_lru_kernel<IPT_Q, IPT_S>);
+        if (e == cudaSuccess) {
+            max_dynamic[dev] = optin - static_cast<int>(fa.sharedSizeBytes);
+            e = cudaFuncSetAttribute(batch_lru_kernel<IPT_Q, IPT_S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     max_dynamic[dev]);
+        }
         if (e != cudaSuccess) {
             cudaGetLastError();  // leave no error behind for the caller's runtime checks
             return ASU_ERR_CUDA_BASE + static_cast<int>(e);
         }
         configured |= 1ull << dev;
     }
-    const size_t smem = static_cast<size_t>(Q) * 4 + S;
+    uint32_t H = 32;
+    while (H < 2 * (Q ? Q : 1)) H <<= 1;
+    const size_t smem = batch_smem_bytes(S, Q, H);
+    if (smem > static_cast<size_t>(max_dynamic[dev])) return ASU_ERR_ARG;
     const uint32_t grid = R < 65535u ? R : 65535u;
-    batch_lru_kernel<IPT_Q, IPT_S><<<grid, kThreads, smem, s>>>(t2s, s2t, lru, q, slot_ids, mask, R, K, S, Q, status);
+    batch_lru_kernel<IPT_Q, IPT_S><<<grid, kThreads, smem, s>>>(t2s, s2t, lru, q, slot_ids, mask, R, K, S, Q, H,
+                                                                 status);
     return asu_launch_status();
 }
 
