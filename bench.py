@@ -114,6 +114,7 @@ def parse_args():
     p.add_argument("--cpu-sample-s", type=float, default=12.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--layers", type=int, default=61, help="decode workload: attention layers per step")
+    p.add_argument("--ops-iters", type=int, default=OPS_ITERS, help="ops workload: timed calls per case (p50 over them)")
     p.add_argument("--host-pitch", type=int, default=0,
                    help="bytes between host-pool rows (0: the pool's default, rows up to 1 KiB padded "
                         "to a multiple of 128 bytes)")
@@ -971,7 +972,7 @@ def run_writeback(args, world: int, rank: int, local_rank: int):
 # ------------------------------------------------------------------ ops lookup / maintain (reference harness)
 
 OPS_REQS = (1, 2, 4, 8)
-OPS_ITERS = 200
+OPS_ITERS = 200  # default of --ops-iters
 
 
 def run_ops(args, world: int, rank: int, local_rank: int):
@@ -996,7 +997,7 @@ def run_ops(args, world: int, rank: int, local_rank: int):
     lookup, maintain = torch.ops.asu.asu_hbm_index_lookup, torch.ops.asu.asu_hbm_index_maintain
     flush = L2Flush(torch, dev)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    iters = max(args.steps, OPS_ITERS)
+    iters = max(args.steps, args.ops_iters)
 
     def timed(restore, op):
         ms = []
