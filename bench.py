@@ -65,6 +65,10 @@ REF_LOOKUP_IDX_PER_S = 50 * 2048 / 350e-6
 SWAPIN_PCIE_READ_BYTES_PER_LAUNCH = 54.31e9 * 652.4e-6   # pcie__read_bytes.sum.per_second x duration
 SWAPIN_NCU_INSTALLS = 0.182 * 128 * 2048                  # rows swapped in by that launch (~18.2% miss)
 LRU_DRAM_BYTES_PER_LAUNCH = 22.05e6 + 0.055e6             # dram__bytes_read.sum + dram__bytes_write.sum
+GATHER_DRAM_BYTES_PER_LAUNCH = 13.82e6                     # lookup workload, gather_vec4_kernel
+RESOLVE_DRAM_BYTES_PER_CALL = 0.383e6                      # decode workload, resolve_kernel
+WRITEBACK_PCIE_WRITE_BYTES_PER_LAUNCH = 59.06e9 * 1.918e-3  # pcie__write_bytes.sum.per_second x duration
+OPS_LOOKUP_DRAM_BYTES_PER_LAUNCH = 0.213e6                  # ops workload, req 8 mixed
 
 
 @dataclass
@@ -646,7 +650,8 @@ def run_lookup(args, world: int, rank: int, local_rank: int):
                      "vs_baseline_note": "per GPU vs 2.93e8 indices/s implied by 50x2048 lookups in 350 us on "
                                          "Ascend 910B (docs/archive/hbm_kvcache_lookup_recommendations.md:32)",
                      "roofline": {"bound": "hbm", "kernel": "gather_vec4_kernel", "achieved": achieved, "peak": hbm,
-                                  "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                                  "unit": "GB/s", "frac": achieved / hbm, "traffic": GATHER_DRAM_BYTES_PER_LAUNCH,
+                                  "traffic_kind": "dram__bytes_read.sum + write.sum of one launch (ncu, this workload)",
                                   "algorithmic_bytes_per_launch": n * 13},
                      "e2e": {"value": world * n * args.steps / (tot_e2e * 1e-3), "unit": UNIT,
                              "h2d_bytes_per_step": n * 4, "d2h_bytes_per_step": n * 5,
@@ -860,7 +865,9 @@ def run_decode(args, world: int, rank: int, local_rank: int):
         "p50_step_us": p50 * 1e3, "p50_call_us": p50 * 1e3 / L,
         "installs_per_step": installs_timed / K, "miss_rate": installs_timed / (K * L * DECODE_TOPK),
         "roofline": {"bound": "hbm", "kernel": "resolve_kernel + resolver_copy_kernel (per layer)",
-                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "traffic": RESOLVE_DRAM_BYTES_PER_CALL * L,
+                     "traffic_kind": "resolve_kernel dram__bytes_read + write per call (ncu, 4-layer case) x layers",
                      "algorithmic_bytes_per_step": alg,
                      "note": "latency-bound: one CTA resolves a 2048-entry top-k; bytes per step are small"},
         "e2e": {"value": idx / (tot_e2e * 1e-3), "unit": UNIT, "h2d_bytes_per_step": L * DECODE_TOPK * 4,
@@ -957,7 +964,9 @@ def run_writeback(args, world: int, rank: int, local_rank: int):
     line.update({"metric": "prefill KV rows written back per second (HBM -> pinned host pool)", "unit": "rows/s",
                  "dtype": "u8", "p50_step_us": p50 * 1e3, "writeback_gbs": achieved,
                  "roofline": {"bound": "host_link", "kernel": "writeback_kernel", "achieved": achieved, "peak": peak,
-                              "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                              "unit": "GB/s", "frac": achieved / peak,
+                              "traffic": WRITEBACK_PCIE_WRITE_BYTES_PER_LAUNCH * L,
+                              "traffic_kind": "PCIe write bytes per launch (ncu pcie__write_bytes, one layer) x layers",
                               "peak_note": "pinned 256 MiB device-to-host cudaMemcpyAsync, best of 10, same run"},
                  "e2e": None, "gpu_launches": L * args.steps,
                  "cpu_baseline": None if not cpu_rows else {
@@ -1144,7 +1153,8 @@ def run_ops(args, world: int, rank: int, local_rank: int):
                                "reports means",
                  "sweep": sweep,
                  "roofline": {"bound": "hbm", "kernel": "ops_lookup_kernel", "achieved": achieved, "peak": hbm,
-                              "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                              "unit": "GB/s", "frac": achieved / hbm, "traffic": OPS_LOOKUP_DRAM_BYTES_PER_LAUNCH,
+                              "traffic_kind": "dram__bytes_read.sum + write.sum of one launch (ncu, req 8 mixed)",
                               "algorithmic_bytes_per_launch": alg,
                               "note": "13 B per query + 12 B per allocation; 8 requests are 8 CTAs: latency-bound"},
                  "e2e": {"value": world * n / (p50_e2e * 1e-3), "unit": UNIT, "h2d_bytes_per_step": n * 4,
