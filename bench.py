@@ -64,7 +64,7 @@ REF_LOOKUP_IDX_PER_S = 50 * 2048 / 350e-6
 # From the ncu captures summarised in profiles/ (first timed step of the resolver workload):
 SWAPIN_PCIE_READ_BYTES_PER_LAUNCH = 54.31e9 * 652.4e-6   # pcie__read_bytes.sum.per_second x duration
 SWAPIN_NCU_INSTALLS = 0.182 * 128 * 2048                  # rows swapped in by that launch (~18.2% miss)
-LRU_DRAM_BYTES_PER_LAUNCH = 22.05e6 + 0.055e6             # dram__bytes_read.sum + dram__bytes_write.sum
+LRU_DRAM_BYTES_PER_LAUNCH = 21.19e6 + 0.062e6             # dram__bytes_read.sum + dram__bytes_write.sum
 GATHER_DRAM_BYTES_PER_LAUNCH = 13.82e6                     # lookup workload, gather_vec4_kernel
 RESOLVE_DRAM_BYTES_PER_CALL = 0.383e6                      # decode workload, resolve_kernel
 WRITEBACK_PCIE_WRITE_BYTES_PER_LAUNCH = 59.06e9 * 1.918e-3  # pcie__write_bytes.sum.per_second x duration
