@@ -1,0 +1,91 @@
+"""vLLM FlashMLA-sparse attention implementation that decodes over the ASU managed cache.
+
+The reference wires its manager into vLLM-Ascend's sparse-attention decode
+(patch/0003 vllm_ascend/attention/sfa_v1.py hunk, patch lines 461-575): a layer whose
+manager holds it, in a decode-only batch of one request and one token, prepares its context
+(reset on a new request, mark the new decode token otherwise), resolves the indexer's top-k
+through ``npu_asu_resolve_kv_slots_single_req`` and runs sparse attention over the managed
+cache with the resolved slots; every other batch takes the original path.
+
+`asu_flashmla_sparse_impl()` returns the same thing for vLLM's FlashMLA-sparse backend on
+B200: a subclass of vLLM's `FlashMLASparseImpl` whose bf16 path, under the reference's
+conditions, replaces the block-table conversion (``triton_convert_req_index_to_global_index``,
+flashmla_sparse.py:755-776) with `sparse_mla.resolve_topk` and points FlashMLA-sparse at the
+managed cache.  fp8_ds_mla caches keep vLLM's path (its fp8 decode kernel reads a paged
+layout).  The manager comes from ``attn_metadata.asu_kv_cache_manager`` as in the reference,
+else from the class attribute ``asu_manager``; the request id from
+``attn_metadata.asu_req_id``, else ``"__single_req__"``::
+
+    Impl = asu_flashmla_sparse_impl()
+    Impl.asu_manager = sparse_mla.contexts_for_mla(kv_caches, max_model_len, block_size)
+    # and build Impl where vLLM builds FlashMLASparseImpl (FlashMLASparseBackend.get_impl_cls)
+"""
+
+from __future__ import annotations
+
+import functools
+
+from . import sparse_mla
+
+SINGLE_REQ_ID = "__single_req__"  # patch line 486
+
+
+def asu_manager_of(impl, attn_metadata):
+    m = getattr(attn_metadata, "asu_kv_cache_manager", None)
+    return m if m is not None else getattr(impl, "asu_manager", None)
+
+
+def use_asu_kv_cache(manager, layer_name: str | None, attn_metadata) -> bool:
+    """patch lines 461-473, with FlashMLA-sparse's metadata: one request, one decode token."""
+    if manager is None or not manager.enabled or layer_name is None or not manager.has_layer(layer_name):
+        return False
+    if getattr(attn_metadata, "max_query_len", None) != 1:
+        return False  # not decode-only
+    if getattr(attn_metadata, "num_reqs", 0) != 1:
+        return False
+    return getattr(attn_metadata, "num_actual_tokens", 0) == 1
+
+
+def prepare_asu_layer_context(manager, layer_name: str, attn_metadata):
+    """patch lines 480-499: reset the manager on a new or shorter request, else mark the token.
+
+    The request's length is ``attn_metadata.max_seq_len`` (a host int: one request).
+    """
+    ctx = manager.get_layer_context(layer_name)
+    actual_seq_len = int(attn_metadata.max_seq_len)
+    req_id = getattr(attn_metadata, "asu_req_id", None) or SINGLE_REQ_ID
+    if ctx.req_id != req_id or ctx.actual_seq_len == 0 or actual_seq_len < ctx.actual_seq_len:
+        managed_prefix_len = max(0, actual_seq_len - attn_metadata.num_actual_tokens)
+        manager.reset_single_request(req_id=req_id, actual_seq_len=actual_seq_len,
+                                     managed_prefix_len=managed_prefix_len,
+                                     original_block_table=attn_metadata.block_table[:1])
+    elif actual_seq_len > ctx.actual_seq_len:
+        manager.mark_decode_token(actual_seq_len - 1)
+    return ctx
+
+
+@functools.lru_cache(maxsize=1)
+def asu_flashmla_sparse_impl():
+    """The subclass, built on first use (vLLM is imported only then)."""
+    from vllm.v1.attention.backends.mla.flashmla_sparse import FlashMLASparseImpl
+
+    class ASUFlashMLASparseImpl(FlashMLASparseImpl):
+        """FlashMLASparseImpl whose single-request bf16 decode reads the ASU managed cache."""
+
+        asu_manager = None
+
+        def forward_mqa(self, q, kv_c_and_k_pe_cache, attn_metadata, layer):
+            self._asu_layer_name = getattr(layer, "layer_name", None)
+            return super().forward_mqa(q, kv_c_and_k_pe_cache, attn_metadata, layer)
+
+        def _forward_bf16_kv(self, q, kv_c_and_k_pe_cache, topk_indices, attn_metadata):
+            manager = asu_manager_of(self, attn_metadata)
+            name = getattr(self, "_asu_layer_name", None)
+            if not use_asu_kv_cache(manager, name, attn_metadata):
+                return super()._forward_bf16_kv(q, kv_c_and_k_pe_cache, topk_indices, attn_metadata)
+            ctx = prepare_asu_layer_context(manager, name, attn_metadata)
+            kv = kv_c_and_k_pe_cache.reshape(*kv_c_and_k_pe_cache.shape[:2], -1)
+            slots = sparse_mla.resolve_topk(ctx, topk_indices.contiguous(), attn_metadata.block_table[0], kv)
+            return self._bf16_flash_mla_kernel(q, sparse_mla.managed_kv_view(ctx), slots)
+
+    return ASUFlashMLASparseImpl

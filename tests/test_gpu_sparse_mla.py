@@ -92,3 +92,53 @@ def test_resolve_topk_fp8_ds_mla_rows_match_oracle():
     np.testing.assert_array_equal(ctx.slot_owner_token.cpu().numpy(), own)
     assert int(ctx.free_slot_count.item()) == int(cnt[0])
     np.testing.assert_array_equal(ctx.managed_kv_cache_0.cpu().numpy(), dst)
+
+
+def _impl(cls, heads, scale, topk_buffer):
+    """An Impl with the fields its bf16 decode reads (no vLLM config is needed for those)."""
+    impl = object.__new__(cls)
+    impl.num_heads, impl.prefill_padding, impl.softmax_scale = heads, 128, scale
+    impl.kv_cache_dtype, impl.topk_indices_buffer = "auto", topk_buffer
+    return impl
+
+
+@pytest.mark.parametrize("heads", [16, 128])
+def test_vllm_subclass_decode_steps_match_stock_flashmla_sparse(heads):
+    """Three decode steps of one request through ASUFlashMLASparseImpl.forward_mqa: each step's
+    output equals vLLM's own FlashMLASparseImpl over the paged cache, the first step resets the
+    manager, the next ones mark the new decode token, and a shared manager serves two layers."""
+    pytest.importorskip("vllm.third_party.flashmla.flash_mla_interface")
+    from types import SimpleNamespace
+
+    from vllm.v1.attention.backends.mla.flashmla_sparse import FlashMLASparseImpl
+
+    from asu_ascend_b200 import sparse_mla as S
+    from asu_ascend_b200 import vllm_backend as V
+
+    seq0, steps, bs, scale = 3000, 3, 64, 576 ** -0.5
+    kv, bt, _ = _case(11, seq0 + steps, tokens=1)
+    kv2 = kv.flip(0).contiguous()  # a second layer's cache
+    g = torch.Generator().manual_seed(12)
+    mgr = S.contexts_for_mla({"layers.0.attn": kv, "layers.1.attn": kv2}, max_seq_len=seq0 + steps, block_size=bs,
+                             managed_slot_count=seq0 + steps, enabled=True)
+    buf = torch.full((1, 2048), -1, dtype=torch.int32, device=DEV)
+    asu = _impl(V.asu_flashmla_sparse_impl(), heads, scale, buf)
+    stock = _impl(FlashMLASparseImpl, heads, scale, buf)
+    for step in range(steps):
+        seq = seq0 + step
+        md = SimpleNamespace(num_reqs=1, max_query_len=1, num_actual_tokens=1, max_seq_len=seq,
+                             block_table=bt.view(1, -1), req_id_per_token=torch.zeros(1, dtype=torch.int32, device=DEV),
+                             block_size=bs, asu_kv_cache_manager=mgr, asu_req_id="req-0")
+        topk = torch.full((2048,), -1, dtype=torch.int32)
+        k = 1900 + 40 * step
+        topk[:k] = torch.randperm(seq, generator=g)[:k].to(torch.int32)
+        topk[0] = seq - 1  # the token this step decodes
+        buf[0].copy_(topk)
+        q = (torch.randn(1, heads, 576, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
+        for name, cache in (("layers.0.attn", kv), ("layers.1.attn", kv2)):
+            got, _ = asu.forward_mqa(q, cache, md, SimpleNamespace(layer_name=name))
+            exp, _ = stock.forward_mqa(q, cache, md, SimpleNamespace(layer_name=name))
+            assert got.shape == exp.shape == (1, heads, 512)
+            torch.testing.assert_close(got.float(), exp.float(), rtol=2e-2, atol=2e-2)
+        ctx = mgr.get_layer_context("layers.1.attn")
+        assert (ctx.req_id, ctx.actual_seq_len, ctx.managed_prefix_len) == ("req-0", seq, seq0 - 1)
