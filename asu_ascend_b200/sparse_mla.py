@@ -30,14 +30,29 @@ def contexts_for_mla(kv_caches: dict[str, torch.Tensor], max_seq_len: int, block
     """Manager over vLLM MLA caches ``[num_blocks, block_size, row]`` (one per layer)."""
     pairs = {name: (c, c.new_empty((*c.shape[:2], 0))) for name, c in kv_caches.items()
              if isinstance(c, torch.Tensor) and c.dim() == 3}
-    return _manager.ASUFullKVCacheManagerFunctional.from_kv_caches(pairs, max_seq_len, block_size,
-                                                                   managed_slot_count, enabled)
+    mgr = _manager.ASUFullKVCacheManagerFunctional.from_kv_caches(pairs, max_seq_len, block_size,
+                                                                  managed_slot_count, enabled)
+    for name in pairs:
+        if mgr.has_layer(name):  # whole pages, so FlashMLA's paged fp8 decode can read it (rows past the slots unused)
+            ctx = mgr.get_layer_context(name)
+            m = ctx.managed_kv_cache_0
+            rows = -(-m.shape[0] // block_size) * block_size
+            if rows != m.shape[0]:
+                ctx.managed_kv_cache_0 = m.new_empty((rows, *m.shape[1:]))
+    return mgr
 
 
 def managed_kv_view(ctx: _manager.ASULayerKVCacheContext) -> torch.Tensor:
     """The managed cache as FlashMLA-sparse's ``kv`` operand: ``[slots, 1, row]``."""
     m = ctx.managed_kv_cache_0
     return m.view(m.shape[0], 1, -1)
+
+
+def managed_paged_view(ctx: _manager.ASULayerKVCacheContext) -> torch.Tensor:
+    """The managed cache as a paged ``[pages, block_size, row]`` cache (slot s = page * block_size
+    + offset), the layout FlashMLA's fp8 sparse decode reads through global slot indices."""
+    m = ctx.managed_kv_cache_0
+    return m.view(-1, ctx.block_size, m.shape[-1])
 
 
 def resolve_topk(ctx: _manager.ASULayerKVCacheContext, topk_indices: torch.Tensor, block_table: torch.Tensor,

@@ -8,11 +8,13 @@ through ``npu_asu_resolve_kv_slots_single_req`` and runs sparse attention over t
 cache with the resolved slots; every other batch takes the original path.
 
 `asu_flashmla_sparse_impl()` returns the same thing for vLLM's FlashMLA-sparse backend on
-B200: a subclass of vLLM's `FlashMLASparseImpl` whose bf16 path, under the reference's
-conditions, replaces the block-table conversion (``triton_convert_req_index_to_global_index``,
-flashmla_sparse.py:755-776) with `sparse_mla.resolve_topk` and points FlashMLA-sparse at the
-managed cache.  fp8_ds_mla caches keep vLLM's path (its fp8 decode kernel reads a paged
-layout).  The manager comes from ``attn_metadata.asu_kv_cache_manager`` as in the reference,
+B200: a subclass of vLLM's `FlashMLASparseImpl` that, under the reference's conditions,
+replaces the block-table conversion (``triton_convert_req_index_to_global_index``,
+flashmla_sparse.py:755-776, 803-812, 898-904) with `sparse_mla.resolve_topk` and points the
+attention kernel at the managed cache: FlashMLA-sparse over ``[slots, 1, 576]`` for bf16
+caches, FlashMLA's fp8 sparse decode over the managed cache seen as pages of ``block_size``
+656-byte fp8_ds_mla rows (both fp8 batch layouts: mixed, and separate prefill/decode).
+The manager comes from ``attn_metadata.asu_kv_cache_manager`` as in the reference,
 else from the class attribute ``asu_manager``; the request id from
 ``attn_metadata.asu_req_id``, else ``"__single_req__"``::
 
@@ -78,14 +80,45 @@ def asu_flashmla_sparse_impl():
             self._asu_layer_name = getattr(layer, "layer_name", None)
             return super().forward_mqa(q, kv_c_and_k_pe_cache, attn_metadata, layer)
 
-        def _forward_bf16_kv(self, q, kv_c_and_k_pe_cache, topk_indices, attn_metadata):
+        def _asu_resolve(self, kv_c_and_k_pe_cache, topk_indices, attn_metadata):
+            """(context, resolved slots) when this batch takes the ASU path, else None."""
             manager = asu_manager_of(self, attn_metadata)
             name = getattr(self, "_asu_layer_name", None)
             if not use_asu_kv_cache(manager, name, attn_metadata):
-                return super()._forward_bf16_kv(q, kv_c_and_k_pe_cache, topk_indices, attn_metadata)
+                return None
             ctx = prepare_asu_layer_context(manager, name, attn_metadata)
             kv = kv_c_and_k_pe_cache.reshape(*kv_c_and_k_pe_cache.shape[:2], -1)
             slots = sparse_mla.resolve_topk(ctx, topk_indices.contiguous(), attn_metadata.block_table[0], kv)
+            return ctx, slots
+
+        def _asu_fp8_decode(self, q, ctx, slots, kernel_metadata):
+            """One decode token: FlashMLA's fp8 sparse decode over the managed pages."""
+            out, _ = self._fp8_flash_mla_kernel(q=q.view(1, 1, *q.shape[1:]),
+                                                kv_c_and_k_pe_cache=sparse_mla.managed_paged_view(ctx),
+                                                topk_indices=slots.view(1, 1, -1), kernel_metadata=kernel_metadata)
+            return out.reshape(q.shape[0], *out.shape[2:])
+
+        def _forward_bf16_kv(self, q, kv_c_and_k_pe_cache, topk_indices, attn_metadata):
+            r = self._asu_resolve(kv_c_and_k_pe_cache, topk_indices, attn_metadata)
+            if r is None:
+                return super()._forward_bf16_kv(q, kv_c_and_k_pe_cache, topk_indices, attn_metadata)
+            ctx, slots = r
             return self._bf16_flash_mla_kernel(q, sparse_mla.managed_kv_view(ctx), slots)
+
+        def _forward_fp8_kv_mixed_batch(self, q, kv_c_and_k_pe_cache, topk_indices, attn_metadata):
+            r = self._asu_resolve(kv_c_and_k_pe_cache, topk_indices, attn_metadata)
+            if r is None:
+                return super()._forward_fp8_kv_mixed_batch(q, kv_c_and_k_pe_cache, topk_indices, attn_metadata)
+            return self._asu_fp8_decode(q, *r, attn_metadata.fp8_extra_metadata)
+
+        def _forward_fp8_kv_separate_prefill_decode(self, q, kv_c_and_k_pe_cache, topk_indices, attn_metadata):
+            meta = attn_metadata.fp8_extra_metadata
+            r = None
+            if getattr(meta, "decode", None) is not None and getattr(meta, "num_prefill_tokens", 1) == 0:
+                r = self._asu_resolve(kv_c_and_k_pe_cache, topk_indices, attn_metadata)
+            if r is None:
+                return super()._forward_fp8_kv_separate_prefill_decode(q, kv_c_and_k_pe_cache, topk_indices,
+                                                                       attn_metadata)
+            return self._asu_fp8_decode(q, *r, meta.decode.kernel_metadata)
 
     return ASUFlashMLASparseImpl

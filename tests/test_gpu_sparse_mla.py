@@ -142,3 +142,78 @@ def test_vllm_subclass_decode_steps_match_stock_flashmla_sparse(heads):
             torch.testing.assert_close(got.float(), exp.float(), rtol=2e-2, atol=2e-2)
         ctx = mgr.get_layer_context("layers.1.attn")
         assert (ctx.req_id, ctx.actual_seq_len, ctx.managed_prefix_len) == ("req-0", seq, seq0 - 1)
+
+
+def _fp8_ds_mla_cache(seed, blocks, bs=64):
+    """Valid 656-byte fp8_ds_mla rows: 512 e4m3 values, 4 f32 scales, 64 bf16 rope values."""
+    g = torch.Generator().manual_seed(seed)
+    n = blocks * bs
+    nope = (torch.randn(n, 512, generator=g) * 2).to(torch.float8_e4m3fn).view(torch.uint8)
+    scales = (torch.rand(n, 4, generator=g) * 0.5 + 0.25).view(torch.uint8)
+    rope = (torch.randn(n, 64, generator=g) * 0.5).to(torch.bfloat16).view(torch.uint8)
+    return torch.cat([nope, scales, rope], 1).view(blocks, bs, 656).to(DEV)
+
+
+@pytest.mark.parametrize("layout", ["mixed", "separate"])
+def test_vllm_subclass_fp8_decode_matches_stock_flashmla(layout):
+    """fp8_ds_mla caches: the subclass decodes with FlashMLA's fp8 sparse decode over the managed
+    pages; each of three steps equals vLLM's stock FlashMLASparseImpl (same kernel over the paged
+    cache) in both fp8 batch layouts, with a managed pool that is not a whole number of pages."""
+    fi = pytest.importorskip("vllm.third_party.flashmla.flash_mla_interface")
+    from types import SimpleNamespace
+
+    from vllm.v1.attention.backends.mla.flashmla_sparse import FlashMLASparseImpl, FlashMLASparseMetadata
+
+    from asu_ascend_b200 import sparse_mla as S
+    from asu_ascend_b200 import vllm_backend as V
+
+    seq0, steps, bs, heads, scale = 2500, 3, 64, 16, 576 ** -0.5
+    nblk = (seq0 + steps + bs - 1) // bs
+    kv = _fp8_ds_mla_cache(21, nblk + 5)
+    g = torch.Generator().manual_seed(22)
+    bt = torch.randperm(nblk + 5, generator=g)[:nblk].to(torch.int32).to(DEV)
+    mgr = S.contexts_for_mla({"layers.0.attn": kv}, max_seq_len=seq0 + steps, block_size=bs,
+                             managed_slot_count=seq0 + steps, enabled=True)
+    assert mgr.get_layer_context("layers.0.attn").managed_kv_cache_0.shape[0] % bs == 0
+    buf = torch.full((1, 2048), -1, dtype=torch.int32, device=DEV)
+    impls = []
+    for cls in (V.asu_flashmla_sparse_impl(), FlashMLASparseImpl):
+        impl = _impl(cls, heads, scale, buf)
+        impl.kv_cache_dtype, impl.fp8_decode_padded_heads, impl.kv_lora_rank = "fp8_ds_mla", 64, 512
+        impls.append(impl)
+
+    def kernel_meta():
+        return FlashMLASparseMetadata.FP8KernelMetadata(
+            scheduler_metadata=fi.get_mla_metadata()[0], dummy_block_table=torch.zeros(1, 1, dtype=torch.int32,
+                                                                                         device=DEV),
+            cache_lens=torch.full((1,), seq0 + steps, dtype=torch.int32, device=DEV))
+
+    def fp8_meta():
+        if layout == "mixed":
+            return kernel_meta()
+        P = FlashMLASparseMetadata.FP8SeparatePrefillDecode
+        return P(num_decodes=1, num_decode_tokens=1,
+                 decode=P.Decode(seq_lens=None, kernel_metadata=kernel_meta(), decode_query_len=1))
+
+    for step in range(steps):
+        seq = seq0 + step
+        topk = torch.full((2048,), -1, dtype=torch.int32)
+        k = 1800 + 50 * step
+        topk[:k] = torch.randperm(seq, generator=g)[:k].to(torch.int32)
+        topk[0] = seq - 1
+        buf[0].copy_(topk)
+        q = (torch.randn(1, heads, 576, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
+        outs = []
+        for impl in impls:
+            md = SimpleNamespace(num_reqs=1, max_query_len=1, num_actual_tokens=1, max_seq_len=seq,
+                                 block_table=bt.view(1, -1),
+                                 req_id_per_token=torch.zeros(1, dtype=torch.int32, device=DEV), block_size=bs,
+                                 asu_kv_cache_manager=mgr, fp8_use_mixed_batch=layout == "mixed",
+                                 fp8_extra_metadata=fp8_meta())
+            outs.append(impl.forward_mqa(q, kv, md, SimpleNamespace(layer_name="layers.0.attn"))[0])
+        got, exp = outs
+        assert got.shape == exp.shape == (1, heads, 512)
+        assert torch.isfinite(exp.float()).all()
+        torch.testing.assert_close(got.float(), exp.float(), rtol=2e-2, atol=2e-2)
+    ctx = mgr.get_layer_context("layers.0.attn")
+    assert (ctx.actual_seq_len, ctx.managed_prefix_len) == (seq0 + steps - 1, seq0 - 1)

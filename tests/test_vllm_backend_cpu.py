@@ -95,3 +95,42 @@ def test_subclass_routes_single_request_decode_to_the_resolver(monkeypatch):
     assert seen == [("resolve", m.ctx["l0"]), ("attn", "managed")]
     assert impl.forward_mqa(q, kv, _md(), SimpleNamespace(layer_name="other")) == ("stock", None)
     assert impl.forward_mqa(q, kv, _md(num_reqs=2), SimpleNamespace(layer_name="l0")) == ("stock", None)
+
+
+def test_subclass_routes_fp8_decode_to_the_resolver(monkeypatch):
+    pytest.importorskip("vllm")
+    Impl = V.asu_flashmla_sparse_impl()
+    from vllm.v1.attention.backends.mla.flashmla_sparse import FlashMLASparseImpl, FlashMLASparseMetadata
+
+    impl = object.__new__(Impl)
+    impl.kv_cache_dtype = "fp8_ds_mla"
+    impl.topk_indices_buffer = torch.zeros(4, 16, dtype=torch.int32)
+    seen = []
+    monkeypatch.setattr(FlashMLASparseImpl, "_forward_fp8_kv_mixed_batch", lambda self, *a: "stock-mixed")
+    monkeypatch.setattr(FlashMLASparseImpl, "_forward_fp8_kv_separate_prefill_decode", lambda self, *a: "stock-sep")
+    monkeypatch.setattr(V.sparse_mla, "resolve_topk", lambda ctx, t, bt, kv: t)
+    monkeypatch.setattr(V.sparse_mla, "managed_paged_view", lambda ctx: "pages")
+
+    def kernel(self, q, kv_c_and_k_pe_cache, topk_indices, kernel_metadata):
+        seen.append((tuple(q.shape), kv_c_and_k_pe_cache, tuple(topk_indices.shape), kernel_metadata))
+        return torch.zeros(1, 1, q.shape[2], 5), None
+
+    monkeypatch.setattr(Impl, "_fp8_flash_mla_kernel", kernel)
+    q, kv = torch.zeros(1, 2, 8), torch.zeros(4, 2, 8)
+    impl.asu_manager = FakeManager()
+    layer = SimpleNamespace(layer_name="l0")
+
+    out, _ = impl.forward_mqa(q, kv, _md(fp8_use_mixed_batch=True, fp8_extra_metadata="km"), layer)
+    assert out.shape == (1, 2, 5) and seen[-1] == ((1, 1, 2, 8), "pages", (1, 1, 16), "km")
+    P = FlashMLASparseMetadata.FP8SeparatePrefillDecode
+    sep = P(num_decodes=1, num_decode_tokens=1, decode=P.Decode(seq_lens=None, kernel_metadata="kd",
+                                                                 decode_query_len=1))
+    out, _ = impl.forward_mqa(q, kv, _md(fp8_use_mixed_batch=False, fp8_extra_metadata=sep), layer)
+    assert out.shape == (1, 2, 5) and seen[-1][3] == "kd"
+    n = len(seen)
+    assert impl.forward_mqa(q, kv, _md(fp8_use_mixed_batch=True, fp8_extra_metadata="km", num_reqs=2),
+                            layer)[0] == "stock-mixed"
+    with_prefill = P(num_decodes=1, num_decode_tokens=1, num_prefill_tokens=3, decode=sep.decode)
+    assert impl.forward_mqa(q, kv, _md(fp8_use_mixed_batch=False, fp8_extra_metadata=with_prefill),
+                            layer)[0] == "stock-sep"
+    assert len(seen) == n
