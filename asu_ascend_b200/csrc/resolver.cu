@@ -134,6 +134,22 @@ __device__ __forceinline__ void block_of(int32_t tok, int64_t bs, int64_t* lb, i
     }
 }
 
+// The global writes of one install: the token's state and slot, the slot's owner (when the
+// popped slot was usable) and its (source row, slot) entry of the install list.
+__device__ __forceinline__ void install_writes(int32_t* token_state, int32_t* hbm_slot, int32_t* owner, int32_t* ws,
+                                               int32_t tok, bool ok, int32_t slot, int32_t src, int64_t entry) {
+    if (ok) {
+        st_cg(token_state + tok, ASU_TOKEN_HBM_RESIDENT);
+        st_cg(hbm_slot + tok, slot);
+        st_cg(owner + slot, tok);
+    }
+    if (entry >= 0) {
+        int32_t* e = ws + 1 + 2 * entry;
+        e[0] = src;
+        e[1] = slot;
+    }
+}
+
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
 resolve_kernel(const int32_t* __restrict__ topk, int64_t n, int32_t* __restrict__ token_state,
                const int32_t* __restrict__ record, int32_t* __restrict__ hbm_slot, int32_t* __restrict__ owner,
@@ -181,7 +197,9 @@ resolve_kernel(const int32_t* __restrict__ topk, int64_t n, int32_t* __restrict_
             if (lb < bt_len) btv = __ldg(block_table + lb);
         }
         cluster_sync_all();  // every table of the cluster cleared
-        int32_t slot = kNotFound;
+        int32_t slot = kNotFound, w_slot = kNotFound, w_src = -1;
+        int64_t w_entry = -1;
+        bool w_ok = false;
         int h = -1;
         int32_t* home_key = nullptr;
         int32_t* home_first = nullptr;
@@ -232,26 +250,30 @@ resolve_kernel(const int32_t* __restrict__ topk, int64_t n, int32_t* __restrict_
             } else {
                 bits |= ASU_ST_FREE_EXHAUSTED;
             }
-            if (ok) {
-                st_cg(token_state + tok, ASU_TOKEN_HBM_RESIDENT);
-                st_cg(hbm_slot + tok, s);
-                st_cg(owner + s, tok);
-            }
             slot = ok ? s : kNotFound;
             home_key[h] = slot;
-            if (c >= 0) {  // a popped entry, usable or not, keeps its place in the install list
-                int32_t* e = ws + 1 + 2 * (n_inst + k);
-                e[0] = ok ? static_cast<int32_t>(src) : -1;
-                e[1] = s;
-            }
+            w_ok = ok;
+            w_slot = s;
+            w_src = ok ? static_cast<int32_t>(src) : -1;
+            w_entry = c >= 0 ? n_inst + k : -1;  // a popped entry, usable or not, keeps its place
         }
+        // The global writes of the last chunk wait until after its final cluster barrier: a
+        // barrier's release would otherwise wait for them to reach L2.  An earlier chunk writes
+        // before its final barrier, whose release/acquire makes the installs visible to the
+        // next chunk's state loads in every CTA.
+        const bool last = base + kChunk >= n;
+        if (!last && canon) install_writes(token_state, hbm_slot, owner, ws, tok, w_ok, w_slot, w_src, w_entry);
         cluster_sync_all();  // first-occurrence slots published
         if (miss && !canon) slot = home_key[h];  // later duplicate of a token installed in this chunk
-        if (pos < n) resolved[pos] = slot;
+        if (!last && pos < n) resolved[pos] = slot;
         const int32_t popped = M < count ? M : (count > 0 ? count : 0);
         count -= popped;
         n_inst += popped;
         cluster_sync_all();  // no CTA reads another's tables any more: next chunk / exit
+        if (last) {
+            if (canon) install_writes(token_state, hbm_slot, owner, ws, tok, w_ok, w_slot, w_src, w_entry);
+            if (pos < n) resolved[pos] = slot;
+        }
     }
     if (rank == 0 && tid == 0) {
         st_cg(count_ptr, count);

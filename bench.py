@@ -869,7 +869,7 @@ def run_decode(args, world: int, rank: int, local_rank: int):
                      "traffic": RESOLVE_DRAM_BYTES_PER_CALL * L,
                      "traffic_kind": "resolve_kernel dram__bytes_read + write per call (ncu, 4-layer case) x layers",
                      "algorithmic_bytes_per_step": alg,
-                     "note": "latency-bound: one CTA resolves a 2048-entry top-k; bytes per step are small"},
+                     "note": "latency-bound: one 8-CTA cluster resolves a 2048-entry top-k; bytes per step are small"},
         "e2e": {"value": idx / (tot_e2e * 1e-3), "unit": UNIT, "h2d_bytes_per_step": L * DECODE_TOPK * 4,
                 "d2h_bytes_per_step": L * DECODE_TOPK * 4,
                 "note": "top-k of all layers copied in, resolved slots copied out, host dispatch of the op included"},
