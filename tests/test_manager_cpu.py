@@ -80,10 +80,13 @@ def test_sparse_mla_contexts_have_one_managed_cache():
     mgr = S.contexts_for_mla(caches, max_seq_len=192, block_size=64, managed_slot_count=50, enabled=True)
     assert mgr.has_layer("layers.0.self_attn") and mgr.has_layer("layers.1.self_attn") and not mgr.has_layer("indexer")
     c0 = mgr.get_layer_context("layers.0.self_attn")
-    assert c0.managed_kv_cache_0.shape == (50, 576) and c0.managed_kv_cache_1.numel() == 0
-    assert S.managed_kv_view(c0).shape == (50, 1, 576)
+    # rows padded to whole 64-row pages for FlashMLA's paged fp8 decode; the state keeps 50 slots
+    assert c0.managed_kv_cache_0.shape == (64, 576) and c0.managed_kv_cache_1.numel() == 0
+    assert c0.slot_owner_token.numel() == 50 and c0.free_slot_stack.numel() == 50
+    assert S.managed_kv_view(c0).shape == (64, 1, 576)
     c1 = mgr.get_layer_context("layers.1.self_attn")
-    assert c1.managed_kv_cache_0.dtype == torch.uint8 and c1.managed_kv_cache_0.shape == (50, 656)
+    assert c1.managed_kv_cache_0.dtype == torch.uint8 and c1.managed_kv_cache_0.shape == (64, 656)
+    assert S.managed_paged_view(c1).shape == (1, 64, 656)
     with pytest.raises(RuntimeError, match="int32"):
         S.resolve_topk(c0, torch.zeros((1, 8), dtype=torch.int64), torch.zeros(3, dtype=torch.int32),
                        caches["layers.0.self_attn"])
