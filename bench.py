@@ -327,6 +327,13 @@ def h2d_peaks(torch, dev, world: int, rank: int) -> tuple[float, float]:
     return alone, concurrent
 
 
+def rank_sync(torch):
+    """The bracket of every timed region: this rank's queued work done, then all ranks together."""
+    torch.cuda.synchronize()
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+
+
 class L2Flush:
     """Write 256 MiB (evicts everything), then read another 256 MiB so the write-back of dirty lines
     happens here, outside the timed region: the next step starts on a cold, clean L2."""
@@ -391,9 +398,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             o = outs[(i * L + layer) % 2]
             pools[layer].step(q_dev[i, layer], out=o)
             host.swapin(recs[layer], q_dev[i, layer], o.slot, o.install, slot_pools[layer], status=status)
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
+    rank_sync(torch)
 
     # per step and layer: [a] resolve [b] swap-in [c]; the free-count snapshots sit outside
     ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(L)] for _ in range(K_steps)]
@@ -417,7 +422,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             host.swapin(recs[layer], q, o.slot, o.install, slot_pools[layer], status=status)
             c.record()
             free_after[k * L + layer] = pools[layer].free_count.sum()
-    torch.cuda.synchronize()
+    rank_sync(torch)
     clk = clocks.stop()
     resolve_ms = [a.elapsed_time(b) for step in ev for a, b, _ in step]
     swapin_ms = [b.elapsed_time(c) for step in ev for _, b, c in step]
@@ -437,6 +442,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     # the two copies run in opposite directions of the host link.
     copy_stream = torch.cuda.Stream(dev)
     main = torch.cuda.current_stream(dev)
+    rank_sync(torch)
     for k in range(K_steps):
         flush()
         torch.cuda._sleep(100_000)
@@ -452,7 +458,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             host.swapin(recs[layer], q_in, o.slot, o.install, slot_pools[layer], status=status)
             main.wait_stream(copy_stream)  # the outputs' buffer is reused two layers later
         ev2[k][1].record()
-    torch.cuda.synchronize()
+    rank_sync(torch)
     e2e_ms = [e[0].elapsed_time(e[1]) for e in ev2]
     for p in pools:
         p.check_status()
@@ -549,6 +555,7 @@ def run_lru1(args, world: int, rank: int, local_rank: int):
     for i in range(base):
         pools.step(q[i])
     ms = []
+    rank_sync(torch)
     for k in range(args.steps):
         flush()
         torch.cuda._sleep(100_000)
@@ -558,6 +565,7 @@ def run_lru1(args, world: int, rank: int, local_rank: int):
         b.record()
         b.synchronize()
         ms.append(a.elapsed_time(b))
+    rank_sync(torch)
     pools.check_status()
     (tot_ms,) = max_over_ranks([sum(ms)], dev)
     cpu = c_oracle.LruPools(1, 131072, 16384, 2048)
@@ -610,7 +618,7 @@ def run_lookup(args, world: int, rank: int, local_rank: int):
     # e2e: the public API with host buffers -- the kernel reads the pinned queries and writes the
     # pinned results itself, so the bytes cross the host link inside the one launch
     H.lookup(tt, q_host, out=out_host, hit=hit_host)
-    torch.cuda.synchronize()
+    rank_sync(torch)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for k in range(args.steps):
         flush()
@@ -627,6 +635,7 @@ def run_lookup(args, world: int, rank: int, local_rank: int):
         b.record()
         b.synchronize()
         ms_e2e.append(a.elapsed_time(b))
+    rank_sync(torch)
     exp, _ = O.gather_lookup(table, query)
     if not (out.cpu().numpy() == exp).all() or not (out_host.numpy() == exp).all():
         raise RuntimeError("lookup output differs from the oracle")
@@ -790,6 +799,7 @@ def run_decode(args, world: int, rank: int, local_rank: int):
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(gpu_index(local_rank))
     clocks.start()
+    rank_sync(torch)
     for k in range(K):
         flush()
         torch.cuda._sleep(sleep_cycles)
@@ -800,6 +810,7 @@ def run_decode(args, world: int, rank: int, local_rank: int):
         b.synchronize()
         ms.append(a.elapsed_time(b))
         advance()
+    rank_sync(torch)
     free_mid = torch.stack([c.free_slot_count for c in ctxs]).sum().item()
     for k in range(K):
         flush()
@@ -813,6 +824,7 @@ def run_decode(args, world: int, rank: int, local_rank: int):
         b.synchronize()
         ms_e2e.append(a.elapsed_time(b))
         advance()
+    rank_sync(torch)
     clock_info = clocks.stop()
     installs_timed = free_before - free_mid
     # parity: replay layer 0 through the oracle (states, slots, last outputs) and check the
@@ -919,7 +931,7 @@ def run_writeback(args, world: int, rank: int, local_rank: int):
 
     for k in range(args.warmup):
         step(k)
-    torch.cuda.synchronize()
+    rank_sync(torch)
     clocks = ClockSampler(gpu_index(local_rank))
     clocks.start()
     ms = []
@@ -931,6 +943,7 @@ def run_writeback(args, world: int, rank: int, local_rank: int):
         b.record()
         b.synchronize()
         ms.append(a.elapsed_time(b))
+    rank_sync(torch)
     clock_info = clocks.stop()
     # the last step's request: every key of layer 3 holds its source row
     last = f"prefill-{rank}-{(args.steps - 1) % 2}"
@@ -1010,6 +1023,7 @@ def run_ops(args, world: int, rank: int, local_rank: int):
 
     def timed(restore, op):
         ms = []
+        rank_sync(torch)
         for i in range(args.warmup + iters):
             restore()
             flush()
@@ -1020,6 +1034,7 @@ def run_ops(args, world: int, rank: int, local_rank: int):
             b.synchronize()
             if i >= args.warmup:
                 ms.append(a.elapsed_time(b))
+        rank_sync(torch)
         return ms
 
     sweep, head = {}, None
@@ -1105,6 +1120,7 @@ def run_ops(args, world: int, rank: int, local_rank: int):
     out_host = torch.empty(q_host.shape, dtype=torch.int32, pin_memory=True)
     q_dev = torch.empty_like(case[4])
     e2e = []
+    rank_sync(torch)
     for i in range(args.warmup + iters):
         for w_, c_ in zip(work[:4], case[:4]):
             w_.copy_(c_)
@@ -1117,6 +1133,7 @@ def run_ops(args, world: int, rank: int, local_rank: int):
         b.synchronize()
         if i >= args.warmup:
             e2e.append(a.elapsed_time(b))
+    rank_sync(torch)
     p50, p50_e2e = statistics.median(ms), statistics.median(e2e)
     p50, p50_e2e = max_over_ranks([p50, p50_e2e], dev)
     if rank != 0:
