@@ -32,6 +32,9 @@
 //     launched with programmatic stream serialization: its CTAs are scheduled while the
 //     resolve cluster runs and wait in griddepcontrol.wait until the resolve grid has
 //     completed and its writes are visible.
+//     Row pairs of up to kInClusterMaxRowBytes whose starts are 16-byte aligned (DSA / MLA
+//     token rows) skip this launch: after each chunk every CTA of the cluster copies the rows
+//     of its own installs, listed in shared memory in rank order.
 // Measured on B200 (16 layers x top-k 2048 per step, L2 flushed per step): ~14.5 us per call
 // for this design and for a single 1024-thread CTA alike, against ~3.5 us for two empty
 // launches; a call is bound by the latency of its dependent steps, not by bandwidth.
@@ -51,6 +54,8 @@ constexpr int kHash = 2 * kChunk;             // per-CTA table: even if every ke
                                               // to one CTA its load factor stays <= 1/2
 constexpr int kCopyThreads = 256;
 constexpr int kCopyUnroll = 4;
+constexpr int64_t kInClusterMaxRowBytes = 1280;  // kv0 + kv1 bytes per token copied by the resolve cluster itself
+constexpr int kInClusterUnroll = 12;             // 16-byte loads in flight per thread in that copy
 constexpr int64_t kMaxRowBytes = 1 << 20;     // kv0 + kv1 bytes per token
 constexpr int64_t kMaxCopyEntries = 2048;     // per copy launch: kMaxCopyEntries * kMaxRowBytes <= 2^31
 
@@ -134,6 +139,42 @@ __device__ __forceinline__ void block_of(int32_t tok, int64_t bs, int64_t* lb, i
     }
 }
 
+// In-cluster copy of one chunk's installs by one CTA: its `m` installs are listed in shared
+// memory in rank order (source row, or -1 for an unusable pop; managed slot), and the CTA's
+// threads walk the flattened (install, 16-byte unit) space of the kv0 + kv1 rows with
+// kInClusterUnroll independent loads in flight per thread.
+__device__ __forceinline__ void copy_installs(const int32_t* s_isrc, const int32_t* s_islot, int m,
+                                              const int4* __restrict__ s0, const int4* __restrict__ s1,
+                                              int4* __restrict__ d0, int4* __restrict__ d1, uint32_t u0, uint32_t u1) {
+    const uint32_t upr = u0 + u1;
+    const uint32_t total = static_cast<uint32_t>(m) * upr;  // <= kThreads * kInClusterMaxRowBytes / 16
+    for (uint32_t base = threadIdx.x; base < total; base += kThreads * kInClusterUnroll) {
+        int4 buf[kInClusterUnroll];
+        int4* dst[kInClusterUnroll];
+#pragma unroll
+        for (int k = 0; k < kInClusterUnroll; ++k) {
+            dst[k] = nullptr;
+            const uint32_t u = base + static_cast<uint32_t>(k) * kThreads;
+            if (u >= total) continue;
+            const uint32_t e = u / upr;
+            const uint32_t ch = u - e * upr;
+            const int64_t src = s_isrc[e];
+            if (src < 0) continue;
+            const int64_t slot = s_islot[e];
+            if (ch < u0) {
+                buf[k] = __ldg(s0 + src * u0 + ch);
+                dst[k] = d0 + slot * u0 + ch;
+            } else {
+                buf[k] = __ldg(s1 + src * u1 + (ch - u0));
+                dst[k] = d1 + slot * u1 + (ch - u0);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kInClusterUnroll; ++k)
+            if (dst[k]) *dst[k] = buf[k];
+    }
+}
+
 // The global writes of one install: the token's state and slot, the slot's owner (when the
 // popped slot was usable) and its (source row, slot) entry of the install list.
 __device__ __forceinline__ void install_writes(int32_t* token_state, int32_t* hbm_slot, int32_t* owner, int32_t* ws,
@@ -156,7 +197,11 @@ resolve_kernel(const int32_t* __restrict__ topk, int64_t n, int32_t* __restrict_
                const int32_t* __restrict__ stack, int32_t* __restrict__ count_ptr, int64_t stack_len,
                const int32_t* __restrict__ block_table, int64_t bt_len, int64_t src_rows, int64_t slot_count,
                int64_t max_seq, int64_t actual, int64_t bs, int32_t* __restrict__ resolved,
-               int32_t* __restrict__ ws, int32_t* status) {
+               int32_t* __restrict__ ws, int32_t* status, const int4* __restrict__ kv0_src,
+               const int4* __restrict__ kv1_src, int4* __restrict__ kv0_dst, int4* __restrict__ kv1_dst, uint32_t u0,
+               uint32_t u1) {
+    // u0 + u1 > 0: this kernel copies the installed rows itself (u0 / u1 16-byte units per
+    // kv0 / kv1 row); 0: the copy kernel launched after it does
     // the copy grid may be scheduled from now on; it waits for this grid's completion itself
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     __shared__ int scan_buf[33];
@@ -164,6 +209,8 @@ resolve_kernel(const int32_t* __restrict__ topk, int64_t n, int32_t* __restrict_
     __shared__ int32_t h_first[kHash];      // first chunk position of the token
     __shared__ int32_t s_stack[kThreads];   // free_slot_stack[count - 1 - (rank * kThreads + t)]
     __shared__ int32_t s_counts[kCluster];  // first occurrences per CTA of the cluster
+    __shared__ int32_t s_isrc[kThreads];    // this CTA's installs of the chunk in rank order: source row
+    __shared__ int32_t s_islot[kThreads];   // ... and managed slot
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = static_cast<int>(cluster.block_rank());
     const int tid = threadIdx.x;
@@ -256,6 +303,8 @@ resolve_kernel(const int32_t* __restrict__ topk, int64_t n, int32_t* __restrict_
             w_slot = s;
             w_src = ok ? static_cast<int32_t>(src) : -1;
             w_entry = c >= 0 ? n_inst + k : -1;  // a popped entry, usable or not, keeps its place
+            s_isrc[local_rank] = w_src;
+            s_islot[local_rank] = s;
         }
         // The global writes of the last chunk wait until after its final cluster barrier: a
         // barrier's release would otherwise wait for them to reach L2.  An earlier chunk writes
@@ -274,6 +323,8 @@ resolve_kernel(const int32_t* __restrict__ topk, int64_t n, int32_t* __restrict_
             if (canon) install_writes(token_state, hbm_slot, owner, ws, tok, w_ok, w_slot, w_src, w_entry);
             if (pos < n) resolved[pos] = slot;
         }
+        // the chunk's rows; the next chunk rewrites the lists only after its third barrier
+        if (u0 + u1 > 0) copy_installs(s_isrc, s_islot, m, kv0_src, kv1_src, kv0_dst, kv1_dst, u0, u1);
     }
     if (rank == 0 && tid == 0) {
         st_cg(count_ptr, count);
@@ -346,12 +397,19 @@ extern "C" int asu_kv_resolver_do(void* stream, const int32_t* topk, int64_t top
     const int vec = (kv0_row_bytes == 0 && kv1_row_bytes == 0) ? 0 : (align & 15) == 0 ? 16 : (align & 3) == 0 ? 4 : 1;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     int32_t* ws = static_cast<int32_t*>(workspace);
+    // Small 16-byte-aligned row pairs (DSA / MLA token rows) are copied by the resolve cluster
+    // as it installs them, which saves the copy launch; larger rows go to the copy kernel,
+    // which spreads them over the whole GPU.
+    const bool in_cluster = vec == 16 && kv0_row_bytes + kv1_row_bytes <= kInClusterMaxRowBytes;
+    const uint32_t u0 = in_cluster ? static_cast<uint32_t>(kv0_row_bytes / 16) : 0;
+    const uint32_t u1 = in_cluster ? static_cast<uint32_t>(kv1_row_bytes / 16) : 0;
     resolve_kernel<<<kCluster, kThreads, 0, s>>>(
         topk, topk_numel, token_state, asu_record_addr, hbm_slot_of_token, slot_owner_token, free_slot_stack,
         free_slot_count, free_slot_stack_len, block_table, block_table_len, src_rows, slot_count, max_seq_len,
-        actual_seq_len, block_size, resolved, ws, status);
+        actual_seq_len, block_size, resolved, ws, status, static_cast<const int4*>(kv0_src),
+        static_cast<const int4*>(kv1_src), static_cast<int4*>(kv0_dst), static_cast<int4*>(kv1_dst), u0, u1);
     int rc = asu_launch_status();
-    if (rc != ASU_OK || vec == 0) return rc;
+    if (rc != ASU_OK || vec == 0 || in_cluster) return rc;
     // one copy launch per kMaxCopyEntries install-list entries (one for any top-k up to that size)
     for (int64_t first = 0; first < topk_numel && rc == ASU_OK; first += kMaxCopyEntries) {
         const int64_t entries = topk_numel - first < kMaxCopyEntries ? topk_numel - first : kMaxCopyEntries;

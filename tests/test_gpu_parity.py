@@ -651,10 +651,11 @@ def test_resolver_multi_chunk_duplicates_match_oracle(n, key_range, seed):
     np.testing.assert_array_equal(N(m1), dst1)
 
 
-@pytest.mark.parametrize("w0,w1", [(3, 5), (2, 6), (8, 0)])
+@pytest.mark.parametrize("w0,w1", [(3, 5), (2, 6), (8, 0), (640, 0), (720, 8)])
 def test_resolver_row_widths_match_oracle(w0, w1):
-    """fp16 rows of 6/10 bytes (byte copies), 4/12 bytes (4-byte copies) and 16 bytes with an
-    empty second cache: the managed rows equal the oracle's byte for byte."""
+    """fp16 rows of 6/10 bytes (byte copies), 4/12 bytes (4-byte copies), 16 and 1280 bytes with
+    an empty second cache (copied by the resolve cluster itself) and 1440 + 16 bytes (16-byte
+    copies by the copy kernel): the managed rows equal the oracle's byte for byte."""
     rng = np.random.Generator(np.random.PCG64(w0 * 10 + w1))
     max_seq, slots, bs, actual, prefix = 4096, 3000, 16, 4000, 3900
     nblk = max_seq // bs
