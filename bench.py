@@ -66,7 +66,7 @@ SWAPIN_PCIE_READ_BYTES_PER_LAUNCH = 54.31e9 * 652.4e-6   # pcie__read_bytes.sum.
 SWAPIN_NCU_INSTALLS = 0.182 * 128 * 2048                  # rows swapped in by that launch (~18.2% miss)
 LRU_DRAM_BYTES_PER_LAUNCH = 21.19e6 + 0.062e6             # dram__bytes_read.sum + dram__bytes_write.sum
 GATHER_DRAM_BYTES_PER_LAUNCH = 13.82e6                     # lookup workload, gather_vec4_kernel
-RESOLVE_DRAM_BYTES_PER_CALL = 0.383e6                      # decode workload, resolve_kernel
+RESOLVE_DRAM_BYTES_PER_CALL = 0.903e6                      # decode workload, resolve_kernel (rows copied in-cluster)
 WRITEBACK_PCIE_WRITE_BYTES_PER_LAUNCH = 59.06e9 * 1.918e-3  # pcie__write_bytes.sum.per_second x duration
 OPS_LOOKUP_DRAM_BYTES_PER_LAUNCH = 0.213e6                  # ops workload, req 8 mixed
 
@@ -876,7 +876,7 @@ def run_decode(args, world: int, rank: int, local_rank: int):
     line.update({
         "p50_step_us": p50 * 1e3, "p50_call_us": p50 * 1e3 / L,
         "installs_per_step": installs_timed / K, "miss_rate": installs_timed / (K * L * DECODE_TOPK),
-        "roofline": {"bound": "hbm", "kernel": "resolve_kernel + resolver_copy_kernel (per layer)",
+        "roofline": {"bound": "hbm", "kernel": "resolve_kernel (per layer; DSA / MLA rows copied by the cluster)",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "traffic": RESOLVE_DRAM_BYTES_PER_CALL * L,
                      "traffic_kind": "resolve_kernel dram__bytes_read + write per call (ncu, 4-layer case) x layers",
@@ -885,7 +885,7 @@ def run_decode(args, world: int, rank: int, local_rank: int):
         "e2e": {"value": idx / (tot_e2e * 1e-3), "unit": UNIT, "h2d_bytes_per_step": L * DECODE_TOPK * 4,
                 "d2h_bytes_per_step": L * DECODE_TOPK * 4,
                 "note": "top-k of all layers copied in, resolved slots copied out, host dispatch of the op included"},
-        "gpu_launches": 2 * L * K,
+        "gpu_launches": L * K,  # one resolve_kernel per call: its 1152-byte bf16 row pairs are copied in-cluster
         "cpu_baseline": None if not calls else {"value": calls * DECODE_TOPK / cpu_s, "unit": UNIT, "cores": 1, "kind": "port",
                          "sample": f"{calls} timed calls (the timed steps of successive layers, each replayed from "
                                    f"a fresh state) of the Python restatement of the reference resolver "
