@@ -427,6 +427,29 @@ def test_lru_many_requests_against_oracle():
     _lru_run_and_compare(pools, oracle, steps, check_state_every=5)
 
 
+@pytest.mark.parametrize("S,Q", [(4096, 4096), (16384, 3000), (1023, 333), (5001, 2049)])
+def test_lru_kernel_shapes_against_oracle(S, Q):
+    """Every thread-work shape of the kernel: 2 or 4 queries and 2 to 16 order entries per
+    thread, the 16384-slot / 4096-query maxima, and slot and query counts that are not
+    multiples of 4 (the order row then moves with 4-byte accesses); duplicates, evictions and
+    shortages on the way."""
+    from asu_ascend_b200.lru import LruSlotPools
+
+    rng = np.random.Generator(np.random.PCG64(S + Q))
+    R, K = 3, 40000
+    tgt = S // 4
+    pools = LruSlotPools(R, K, S, tgt, Q, device=DEV)
+    oracle = [O.LruPool(S, tgt) for _ in range(R)]
+    hot = rng.integers(0, K, (R, 2 * S))
+    steps = []
+    for _ in range(8):
+        q = np.empty((R, Q), np.int32)
+        for r in range(R):
+            q[r] = np.where(rng.random(Q) < 0.8, rng.choice(hot[r], Q), rng.integers(0, K, Q))
+        steps.append(q)
+    _lru_run_and_compare(pools, oracle, steps, check_state_every=3)
+
+
 def test_lru_c2_shape_against_oracle():
     """128 requests, 128K keys, 8192 slots, target 2048, top-k 2048 with c0 locality: 6 steps."""
     from asu_ascend_b200.lru import LruSlotPools
