@@ -328,6 +328,42 @@ def test_batch_lru_through_reference_c_launcher():
     np.testing.assert_array_equal(N(tl)[0], e_lru)
 
 
+@pytest.mark.parametrize("S,Q,R", [(37, 5, 3), (1000, 300, 4), (4100, 2048, 2), (10240, 1536, 5)])
+def test_batch_lru_random_states_against_oracle(S, Q, R):
+    """Slot counts from 37 to 10240 (every thread-work shape of the kernel), partly empty slot
+    tables, queries with duplicates, -1 and out-of-range ids, four rounds per request."""
+    rng = np.random.Generator(np.random.PCG64(S * 7 + Q))
+    K = 3 * S
+    t2s = np.full((R, K), -1, np.int32)
+    s2t = np.full((R, S), -1, np.int32)
+    lru = np.empty((R, S), np.int16)
+    for r in range(R):
+        resident = rng.choice(K, int(S * 0.8), replace=False)
+        slots = rng.choice(S, len(resident), replace=False)
+        t2s[r, resident] = slots
+        s2t[r, slots] = resident
+        lru[r] = rng.permutation(S).astype(np.int16)
+    tt, ts, tl = T(t2s), T(s2t), T(lru)
+    state = [[t2s[r].tolist(), s2t[r].tolist(), lru[r].astype(np.int32).tolist()] for r in range(R)]
+    for _ in range(4):
+        q = np.empty((R, Q), np.int32)
+        for r in range(R):
+            res = [t for t, sl in enumerate(state[r][0]) if sl >= 0]
+            # at most S // 4 distinct misses: always enough victims
+            pool = np.concatenate([rng.choice(res, Q), rng.integers(0, K, max(1, S // 8))])
+            q[r] = rng.choice(pool, Q)
+            q[r, rng.random(Q) < 0.02] = -1
+            q[r, rng.random(Q) < 0.01] = K + 5
+        sid, mask = torch.ops.asu.asu_hbm_index_lookup_simt(tt, ts, tl, T(q), R)
+        for r in range(R):
+            es, em = O.batch_lru(q[r].tolist(), *state[r])
+            np.testing.assert_array_equal(N(sid)[r], es)
+            np.testing.assert_array_equal(N(mask)[r], em)
+            np.testing.assert_array_equal(N(tt)[r], state[r][0])
+            np.testing.assert_array_equal(N(ts)[r], state[r][1])
+            np.testing.assert_array_equal(N(tl)[r].astype(np.int32), state[r][2])
+
+
 def test_batch_lru_no_victim_leaves_state_unchanged():
     from asu_ascend_b200._lib import AsuError
 
