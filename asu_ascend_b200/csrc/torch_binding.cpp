@@ -1,5 +1,6 @@
-// C++ torch binding of npu_asu_resolve_kv_slots_single_req, the op a decode step calls once per
-// layer.
+// C++ torch binding of the hot-path operators: npu_asu_resolve_kv_slots_single_req, the op a
+// decode step calls once per layer, and the index operators asu_hbm_index_lookup,
+// asu_hbm_index_maintain and asu_hbm_index_lookup_simt.
 //
 // Reference interface: patch/0001 csrc/torch_binding.cpp hunk (patch lines 810-826, schema) and
 // csrc/asu_kv_resolver/asu_kv_resolver_torch_adpt.h (patch lines 21-59): TORCH_LIBRARY_FRAGMENT
@@ -8,9 +9,20 @@
 // there is no CPU implementation) and Meta kernels.  The argument checks and their error types
 // (ValueError / RuntimeError) are the ones the Python reference raises (patch lines 954-994).
 //
-// Why C++: the op is on the per-layer decode path, and a Python kernel spends tens of
+// Index operators: ascend-ops/torch_binding_asu_hbm_index.cpp:7-25 (schemas under _C_ascend)
+// and the adapters asu_hbm_index_lookup/asu_hbm_index_lookup_torch_adpt.h:15-35 and
+// asu_hbm_index_maintain/asu_hbm_index_maintain_torch_adpt.h (the int32 dtype checks, then
+// req_num > 0, then slot_out = empty_like(query_index)); the device, contiguity and row-width
+// checks the raw pointers need follow.  The batch-LRU operator has no torch binding in the
+// reference (pta-ops/asu_hbm_index_lookup_simt calls its C launcher through ctypes); it is
+// registered here with the same conventions.
+//
+// Why C++: the ops are on the per-layer decode path, and a Python kernel spends tens of
 // microseconds per call on argument handling; here a call costs a few microseconds of host time
-// on top of its two launches.  The kernels are reached through the C ABI (asu_kv_resolver_do).
+// on top of its launches.  The kernels are reached through the C ABI (asu_kv_resolver_do,
+// asu_hbm_index_*_ex).  A device status word is allocated, read back and turned into an error
+// only while status checks are on; otherwise the launches get no status pointer and the ops stay
+// asynchronous, like the NPU ones.
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
@@ -18,6 +30,7 @@
 
 #include <atomic>
 #include <sstream>
+#include <tuple>
 #include <string>
 
 #include "../../include/asu_b200.h"
@@ -179,6 +192,171 @@ at::Tensor resolve_meta(const at::Tensor& original_topk_indices, int64_t, int64_
     return at::empty(original_topk_indices.sizes(), original_topk_indices.options().dtype(at::kInt));
 }
 
+// ---------------------------------------------------------------------------------------------
+// index operators
+
+int64_t row_width(const char* name, const at::Tensor& t, int64_t req_num) {
+    TORCH_CHECK(t.numel() % req_num == 0, name, " has ", t.numel(), " elements, not a multiple of req_num=", req_num);
+    const int64_t w = t.numel() / req_num;
+    TORCH_CHECK(w <= 0x7fffffff, name, " rows are too long (", w, " elements)");
+    return w;
+}
+
+void check_int32(const char* name, const at::Tensor& t) {
+    TORCH_CHECK(t.scalar_type() == at::kInt, name, " must be int32");
+}
+
+// Status word of one launch: allocated only while checks are on.
+at::Tensor new_status(int64_t req_num, const at::Tensor& like) {
+    return g_status_checks.load(std::memory_order_relaxed) ? at::zeros({req_num}, like.options().dtype(at::kInt))
+                                                            : at::Tensor();
+}
+
+void launch_ok(int rc, const char* what) {
+    TORCH_CHECK(rc == ASU_OK, what, " failed: ", asu_status_string(rc), " (code ", rc, ")");
+}
+
+// Reads the status words back (a synchronisation) and raises on any bit but SHORTAGE, which the
+// statistics count.
+void raise_on_status(const at::Tensor& status, const char* what) {
+    if (!status.defined()) return;
+    const at::Tensor host = status.cpu();
+    const int32_t* p = host.data_ptr<int32_t>();
+    int bits = 0;
+    for (int64_t i = 0; i < host.numel(); ++i) bits |= p[i];
+    bits &= ~ASU_ST_SHORTAGE;
+    if (bits != 0) {
+        std::ostringstream hex;
+        hex << std::hex << bits;
+        TORCH_CHECK(false, what, ": device status ", status_list(bits), " (0x", hex.str(), ")");
+    }
+}
+
+int32_t* status_ptr(const at::Tensor& status) { return status.defined() ? status.data_ptr<int32_t>() : nullptr; }
+
+// The reference adapter's checks, in its order, then the pointer contract.
+void index_op_checks(const char* const* names, const at::Tensor* const* ts, int n, int64_t req_num) {
+    for (int i = 0; i < n; ++i) check_int32(names[i], *ts[i]);
+    TORCH_CHECK(req_num > 0, "req_num must be greater than 0");
+    const c10::Device dev = ts[0]->device();
+    for (int i = 0; i < n; ++i) req_cuda_i32(names[i], *ts[i], dev);
+}
+
+at::Tensor lookup_cuda(at::Tensor& index, at::Tensor& slot_to_index, at::Tensor& free_slots, at::Tensor& free_head,
+                       const at::Tensor& query_index, int64_t req_num) {
+    const char* names[] = {"index", "slot_to_index", "free_slots", "free_head", "query_index"};
+    const at::Tensor* ts[] = {&index, &slot_to_index, &free_slots, &free_head, &query_index};
+    index_op_checks(names, ts, 5, req_num);
+    TORCH_CHECK(free_head.numel() >= req_num, "free_head must hold req_num entries");
+    const c10::cuda::CUDAGuard guard(index.device());
+    at::Tensor slot_out = at::empty_like(query_index);
+    const at::Tensor status = new_status(req_num, index);
+    launch_ok(asu_hbm_index_lookup_ex(
+                  c10::cuda::getCurrentCUDAStream(index.device().index()).stream(), index.data_ptr<int32_t>(),
+                  slot_to_index.data_ptr<int32_t>(), free_slots.data_ptr<int32_t>(), free_head.data_ptr<int32_t>(),
+                  query_index.data_ptr<int32_t>(), slot_out.data_ptr<int32_t>(), static_cast<uint32_t>(req_num),
+                  row_width("index", index, req_num), row_width("slot_to_index", slot_to_index, req_num),
+                  row_width("free_slots", free_slots, req_num), row_width("query_index", query_index, req_num),
+                  status_ptr(status)),
+              "asu_hbm_index_lookup");
+    raise_on_status(status, "asu_hbm_index_lookup");
+    return slot_out;
+}
+
+void maintain_cuda(at::Tensor& index, at::Tensor& slot_to_index, at::Tensor& free_slots, at::Tensor& free_head,
+                   const at::Tensor& last_query_slots, int64_t req_num, int64_t seed) {
+    const char* names[] = {"index", "slot_to_index", "free_slots", "free_head", "last_query_slots"};
+    const at::Tensor* ts[] = {&index, &slot_to_index, &free_slots, &free_head, &last_query_slots};
+    index_op_checks(names, ts, 5, req_num);
+    TORCH_CHECK(free_head.numel() >= req_num, "free_head must hold req_num entries");
+    const c10::cuda::CUDAGuard guard(index.device());
+    const at::Tensor status = new_status(req_num, index);
+    launch_ok(asu_hbm_index_maintain_ex(
+                  c10::cuda::getCurrentCUDAStream(index.device().index()).stream(), index.data_ptr<int32_t>(),
+                  slot_to_index.data_ptr<int32_t>(), free_slots.data_ptr<int32_t>(), free_head.data_ptr<int32_t>(),
+                  last_query_slots.data_ptr<int32_t>(), static_cast<uint32_t>(req_num),
+                  static_cast<uint32_t>(seed & 0xFFFFFFFF), row_width("index", index, req_num),
+                  row_width("slot_to_index", slot_to_index, req_num), row_width("free_slots", free_slots, req_num),
+                  row_width("last_query_slots", last_query_slots, req_num), status_ptr(status)),
+              "asu_hbm_index_maintain");
+    raise_on_status(status, "asu_hbm_index_maintain");
+}
+
+std::tuple<at::Tensor, at::Tensor> simt_cuda(at::Tensor& token_to_slot, at::Tensor& slot_to_token,
+                                             at::Tensor& lru_slots, const at::Tensor& query_token_ids,
+                                             int64_t req_num) {
+    const char* names[] = {"token_to_slot", "slot_to_token", "query_token_ids"};
+    const at::Tensor* ts[] = {&token_to_slot, &slot_to_token, &query_token_ids};
+    TORCH_CHECK(lru_slots.scalar_type() == at::kShort, "lru_slots must be int16");
+    index_op_checks(names, ts, 3, req_num);
+    TORCH_CHECK(lru_slots.device() == token_to_slot.device() && lru_slots.is_contiguous(),
+                "lru_slots must be a contiguous int16 tensor on the same device");
+    const c10::cuda::CUDAGuard guard(token_to_slot.device());
+    at::Tensor slot_ids = at::empty_like(query_token_ids);
+    at::Tensor miss_mask = at::empty(query_token_ids.sizes(), query_token_ids.options().dtype(at::kBool));
+    const at::Tensor status = new_status(req_num, token_to_slot);
+    launch_ok(asu_hbm_index_lookup_simt_ex(
+                  c10::cuda::getCurrentCUDAStream(token_to_slot.device().index()).stream(),
+                  token_to_slot.data_ptr<int32_t>(), slot_to_token.data_ptr<int32_t>(),
+                  lru_slots.data_ptr<int16_t>(), query_token_ids.data_ptr<int32_t>(), slot_ids.data_ptr<int32_t>(),
+                  reinterpret_cast<uint8_t*>(miss_mask.data_ptr<bool>()), static_cast<uint32_t>(req_num),
+                  row_width("token_to_slot", token_to_slot, req_num), row_width("slot_to_token", slot_to_token, req_num),
+                  row_width("query_token_ids", query_token_ids, req_num), status_ptr(status)),
+              "asu_hbm_index_lookup_simt");
+    raise_on_status(status, "asu_hbm_index_lookup_simt");
+    return {slot_ids, miss_mask};
+}
+
+// Host tensors: the same checks (the first failing one reports host memory), then a refusal.
+at::Tensor lookup_cpu(at::Tensor& index, at::Tensor& slot_to_index, at::Tensor& free_slots, at::Tensor& free_head,
+                      const at::Tensor& query_index, int64_t req_num) {
+    const char* names[] = {"index", "slot_to_index", "free_slots", "free_head", "query_index"};
+    const at::Tensor* ts[] = {&index, &slot_to_index, &free_slots, &free_head, &query_index};
+    index_op_checks(names, ts, 5, req_num);
+    TORCH_CHECK(false, "asu_hbm_index_lookup needs CUDA tensors");
+}
+
+void maintain_cpu(at::Tensor& index, at::Tensor& slot_to_index, at::Tensor& free_slots, at::Tensor& free_head,
+                  const at::Tensor& last_query_slots, int64_t req_num, int64_t) {
+    const char* names[] = {"index", "slot_to_index", "free_slots", "free_head", "last_query_slots"};
+    const at::Tensor* ts[] = {&index, &slot_to_index, &free_slots, &free_head, &last_query_slots};
+    index_op_checks(names, ts, 5, req_num);
+    TORCH_CHECK(false, "asu_hbm_index_maintain needs CUDA tensors");
+}
+
+std::tuple<at::Tensor, at::Tensor> simt_cpu(at::Tensor& token_to_slot, at::Tensor& slot_to_token,
+                                            at::Tensor& lru_slots, const at::Tensor& query_token_ids,
+                                            int64_t req_num) {
+    const char* names[] = {"token_to_slot", "slot_to_token", "query_token_ids"};
+    const at::Tensor* ts[] = {&token_to_slot, &slot_to_token, &query_token_ids};
+    TORCH_CHECK(lru_slots.scalar_type() == at::kShort, "lru_slots must be int16");
+    index_op_checks(names, ts, 3, req_num);
+    TORCH_CHECK(false, "asu_hbm_index_lookup_simt needs CUDA tensors");
+}
+
+at::Tensor lookup_meta(at::Tensor&, at::Tensor&, at::Tensor&, at::Tensor&, const at::Tensor& query_index, int64_t) {
+    return at::empty_like(query_index);
+}
+
+void maintain_meta(at::Tensor&, at::Tensor&, at::Tensor&, at::Tensor&, const at::Tensor&, int64_t, int64_t) {}
+
+std::tuple<at::Tensor, at::Tensor> simt_meta(at::Tensor&, at::Tensor&, at::Tensor&, const at::Tensor& query_token_ids,
+                                             int64_t) {
+    return {at::empty_like(query_token_ids), at::empty(query_token_ids.sizes(), query_token_ids.options().dtype(at::kBool))};
+}
+
+constexpr const char* kLookupSchema =
+    "asu_hbm_index_lookup(Tensor(a!) index, Tensor(b!) slot_to_index, Tensor(c!) free_slots, Tensor(d!) free_head, "
+    "Tensor query_index, int req_num) -> Tensor";
+constexpr const char* kMaintainSchema =
+    "asu_hbm_index_maintain(Tensor(a!) index, Tensor(b!) slot_to_index, Tensor(c!) free_slots, Tensor(d!) free_head, "
+    "Tensor last_query_slots, int req_num, int seed) -> ()";
+constexpr const char* kSimtSchema =
+    "asu_hbm_index_lookup_simt(Tensor(a!) token_to_slot, Tensor(b!) slot_to_token, Tensor(c!) lru_slots, "
+    "Tensor query_token_ids, int req_num) -> (Tensor, Tensor)";
+
+// ---------------------------------------------------------------------------------------------
+
 constexpr const char* kSchema =
     "npu_asu_resolve_kv_slots_single_req(Tensor original_topk_indices, int actual_seq_len, int managed_prefix_len, "
     "Tensor! token_state, Tensor asu_record_addr, Tensor! hbm_slot_of_token, Tensor! slot_owner_token, "
@@ -187,15 +365,26 @@ constexpr const char* kSchema =
 
 }  // namespace
 
-TORCH_LIBRARY_FRAGMENT(asu, m) { m.def(kSchema); }
-TORCH_LIBRARY_FRAGMENT(_C_ascend, m) { m.def(kSchema); }
+#define ASU_DEFINE_OPS(m)    \
+    m.def(kSchema);          \
+    m.def(kLookupSchema);    \
+    m.def(kMaintainSchema);  \
+    m.def(kSimtSchema);
+#define ASU_IMPL_OPS(m, resolve, lookup, maintain, simt)         \
+    m.impl("npu_asu_resolve_kv_slots_single_req", &resolve);     \
+    m.impl("asu_hbm_index_lookup", &lookup);                     \
+    m.impl("asu_hbm_index_maintain", &maintain);                 \
+    m.impl("asu_hbm_index_lookup_simt", &simt);
 
-TORCH_LIBRARY_IMPL(asu, CUDA, m) { m.impl("npu_asu_resolve_kv_slots_single_req", &resolve_cuda); }
-TORCH_LIBRARY_IMPL(_C_ascend, CUDA, m) { m.impl("npu_asu_resolve_kv_slots_single_req", &resolve_cuda); }
-TORCH_LIBRARY_IMPL(asu, CPU, m) { m.impl("npu_asu_resolve_kv_slots_single_req", &resolve_cpu); }
-TORCH_LIBRARY_IMPL(_C_ascend, CPU, m) { m.impl("npu_asu_resolve_kv_slots_single_req", &resolve_cpu); }
-TORCH_LIBRARY_IMPL(asu, Meta, m) { m.impl("npu_asu_resolve_kv_slots_single_req", &resolve_meta); }
-TORCH_LIBRARY_IMPL(_C_ascend, Meta, m) { m.impl("npu_asu_resolve_kv_slots_single_req", &resolve_meta); }
+TORCH_LIBRARY_FRAGMENT(asu, m) { ASU_DEFINE_OPS(m) }
+TORCH_LIBRARY_FRAGMENT(_C_ascend, m) { ASU_DEFINE_OPS(m) }
+
+TORCH_LIBRARY_IMPL(asu, CUDA, m) { ASU_IMPL_OPS(m, resolve_cuda, lookup_cuda, maintain_cuda, simt_cuda) }
+TORCH_LIBRARY_IMPL(_C_ascend, CUDA, m) { ASU_IMPL_OPS(m, resolve_cuda, lookup_cuda, maintain_cuda, simt_cuda) }
+TORCH_LIBRARY_IMPL(asu, CPU, m) { ASU_IMPL_OPS(m, resolve_cpu, lookup_cpu, maintain_cpu, simt_cpu) }
+TORCH_LIBRARY_IMPL(_C_ascend, CPU, m) { ASU_IMPL_OPS(m, resolve_cpu, lookup_cpu, maintain_cpu, simt_cpu) }
+TORCH_LIBRARY_IMPL(asu, Meta, m) { ASU_IMPL_OPS(m, resolve_meta, lookup_meta, maintain_meta, simt_meta) }
+TORCH_LIBRARY_IMPL(_C_ascend, Meta, m) { ASU_IMPL_OPS(m, resolve_meta, lookup_meta, maintain_meta, simt_meta) }
 
 // Status checks of the op (synchronise after each call and raise on a device status); the Python
 // side's ops.set_status_checks() forwards here.
