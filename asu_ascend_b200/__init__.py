@@ -3,9 +3,14 @@
 Submodules (importing any of the CUDA-backed ones loads libasu_b200.so and fails loudly
 if it is not built -- there is no CPU fallback):
 
-* ``ops``               torch operators with the reference schemas, under torch.ops.asu and
-                        torch.ops._C_ascend (asu_hbm_index_lookup / _maintain / _lookup_simt,
-                        npu_asu_resolve_kv_slots_single_req)
+* ``ops``               loads the C++ torch operators with the reference schemas, under
+                        torch.ops.asu and torch.ops._C_ascend (asu_hbm_index_lookup / _maintain /
+                        _lookup_simt, npu_asu_resolve_kv_slots_single_req)
+* ``manager``           per-layer single-request resolver state (patch/0003 manager)
+* ``sparse_mla``        resolver slots for vLLM's FlashMLA-sparse decode
+* ``vllm_backend``      FlashMLASparseImpl subclass that decodes over the managed cache
+* ``kv_store``          MicroKV-keyed view of the host row pool (prefill write-back)
+* ``kv_server``         MicroKV socket protocol in front of that store
 * ``hbm_lookup_update`` mirror of the reference's gather/update extension module
 * ``lru``               per-request exact-LRU slot pools (LruSlotPools)
 * ``host_pool``         pinned mapped host row pool + swap-in gather (HostRowPool)
