@@ -238,6 +238,7 @@ int32_t* status_ptr(const at::Tensor& status) { return status.defined() ? status
 void index_op_checks(const char* const* names, const at::Tensor* const* ts, int n, int64_t req_num) {
     for (int i = 0; i < n; ++i) check_int32(names[i], *ts[i]);
     TORCH_CHECK(req_num > 0, "req_num must be greater than 0");
+    TORCH_CHECK(req_num <= 0x7fffffff, "req_num must fit in int32");
     const c10::Device dev = ts[0]->device();
     for (int i = 0; i < n; ++i) req_cuda_i32(names[i], *ts[i], dev);
 }
