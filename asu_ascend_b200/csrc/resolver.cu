@@ -202,7 +202,11 @@ resolve_kernel(const int32_t* __restrict__ topk, int64_t n, int32_t* __restrict_
                uint32_t u1) {
     // u0 + u1 > 0: this kernel copies the installed rows itself (u0 / u1 16-byte units per
     // kv0 / kv1 row); 0: the copy kernel launched after it does
-    // the copy grid may be scheduled from now on; it waits for this grid's completion itself
+    // Launched as a programmatic dependent: the CTAs may be resident before the previous grid on
+    // the stream has finished; nothing is read before it has completed and its writes are visible.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // the next grid (the copy kernel, or the next resolve) may be scheduled from now on; it
+    // waits for this grid's completion itself
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     __shared__ int scan_buf[33];
     __shared__ int32_t h_key[kHash];        // token id; reused for the installed slot after ranking
@@ -403,11 +407,29 @@ extern "C" int asu_kv_resolver_do(void* stream, const int32_t* topk, int64_t top
     const bool in_cluster = vec == 16 && kv0_row_bytes + kv1_row_bytes <= kInClusterMaxRowBytes;
     const uint32_t u0 = in_cluster ? static_cast<uint32_t>(kv0_row_bytes / 16) : 0;
     const uint32_t u1 = in_cluster ? static_cast<uint32_t>(kv1_row_bytes / 16) : 0;
-    resolve_kernel<<<kCluster, kThreads, 0, s>>>(
-        topk, topk_numel, token_state, asu_record_addr, hbm_slot_of_token, slot_owner_token, free_slot_stack,
-        free_slot_count, free_slot_stack_len, block_table, block_table_len, src_rows, slot_count, max_seq_len,
-        actual_seq_len, block_size, resolved, ws, status, static_cast<const int4*>(kv0_src),
-        static_cast<const int4*>(kv1_src), static_cast<int4*>(kv0_dst), static_cast<int4*>(kv1_dst), u0, u1);
+    {
+        // programmatic stream serialization: the cluster is scheduled while the previous grid
+        // drains (the kernel's griddepcontrol.wait keeps stream order for its memory accesses)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(kCluster);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = 0;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t e = cudaLaunchKernelEx(
+            &cfg, resolve_kernel, topk, topk_numel, token_state, asu_record_addr, hbm_slot_of_token, slot_owner_token,
+            free_slot_stack, free_slot_count, free_slot_stack_len, block_table, block_table_len, src_rows, slot_count,
+            max_seq_len, actual_seq_len, block_size, resolved, ws, status, static_cast<const int4*>(kv0_src),
+            static_cast<const int4*>(kv1_src), static_cast<int4*>(kv0_dst), static_cast<int4*>(kv1_dst), u0, u1);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return ASU_ERR_CUDA_BASE + static_cast<int>(e);
+        }
+    }
     int rc = asu_launch_status();
     if (rc != ASU_OK || vec == 0 || in_cluster) return rc;
     // one copy launch per kMaxCopyEntries install-list entries (one for any top-k up to that size)
