@@ -33,6 +33,34 @@ __host__ __device__ __forceinline__ uint32_t hash32(uint32_t x) {
 __device__ __forceinline__ int32_t ld_cg(const int32_t* p) { return __ldcg(p); }
 __device__ __forceinline__ void st_cg(int32_t* p, int32_t v) { __stcg(p, v); }
 
+// Programmatic dependent launch (PDL).  A kernel launched with launch_pdl() may have its CTAs
+// scheduled while the previous grid on the stream is still draining; it calls pdl_wait() before
+// its first global-memory access, which returns once that grid has completed and its writes are
+// visible, so stream order holds.  pdl_trigger() lets the next PDL grid be scheduled early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                      Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return ASU_ERR_CUDA_BASE + static_cast<int>(e);
+    }
+    return ASU_OK;
+}
+
 __device__ __forceinline__ void flag_status(int32_t* status, int row, int32_t bits) {
     if (status != nullptr) atomicOr(status + row, bits);
 }

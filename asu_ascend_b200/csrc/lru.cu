@@ -54,6 +54,8 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
                 int32_t* __restrict__ evicted, uint32_t ev_stride, int32_t* __restrict__ ev_count,
                 int64_t* __restrict__ stats, int32_t* status, uint32_t req_num, uint32_t K, uint32_t S, uint32_t Q,
                 uint32_t target, int log2h) {
+    pdl_wait();     // launched with launch_pdl: stream order for every access below
+    pdl_trigger();  // the swap-in that consumes this step may be scheduled now
     extern __shared__ int32_t smem[];
     const uint32_t H = 1u << log2h;
     const uint32_t Sp = (S + 3) & ~3u;  // row length rounded up to 16 bytes
@@ -445,10 +447,9 @@ int launch_lru(cudaStream_t s, int32_t* t2s, int32_t* s2t, int32_t* order, int32
     }
     if (smem > static_cast<size_t>(max_dynamic[dev])) return ASU_ERR_ARG;
     const uint32_t grid = R < 65535u ? R : 65535u;
-    lru_step_kernel<IPT_Q, IPT_S><<<grid, kThreads, smem, s>>>(t2s, s2t, order, stack, count, query, slot_out, hit,
-                                                                 inst, evicted, ev_stride, ev_count, stats, status,
-                                                                 R, K, S, Q, target, log2h);
-    return asu_launch_status();
+    return launch_pdl(lru_step_kernel<IPT_Q, IPT_S>, dim3(grid), dim3(kThreads), smem, s, t2s, s2t, order, stack,
+                      count, query, slot_out, hit, inst, evicted, ev_stride, ev_count, stats, status, R, K, S, Q,
+                      target, log2h);
 }
 
 template <int IPT_Q>

@@ -29,6 +29,8 @@ swapin_kernel(const int4* host, int64_t pool_rows, uint32_t cpr, uint32_t pitch1
               const int32_t* __restrict__ slot,
               const uint8_t* __restrict__ inst, uint32_t Q, int4* __restrict__ pool, uint32_t S, uint32_t R,
               int32_t* status) {
+    pdl_wait();     // launched with launch_pdl: the masks and slots of the step before are visible
+    pdl_trigger();
     __shared__ int64_t src_row[kWarps][32];
     __shared__ int64_t dst_row[kWarps][32];
     const int lane = threadIdx.x & 31;
@@ -133,6 +135,8 @@ swapin_bulk_kernel(const uint8_t* host, int64_t pool_rows, uint32_t row_bytes, u
                    const int32_t* __restrict__ rec, uint32_t K, const int32_t* __restrict__ query,
                    const int32_t* __restrict__ slot, const uint8_t* __restrict__ inst, uint32_t Q,
                    uint8_t* __restrict__ pool, uint32_t S, uint32_t R, int32_t* status, uint32_t slot_stride) {
+    pdl_wait();     // launched with launch_pdl: the masks and slots of the step before are visible
+    pdl_trigger();
     extern __shared__ __align__(128) uint8_t slots[];
     __shared__ __align__(8) uint64_t bars[kBulkWarps * 32];
     const int lane = threadIdx.x & 31;
@@ -249,17 +253,17 @@ extern "C" int asu_swapin_gather(void* stream, const void* host_pool, int64_t po
         uint64_t grid = (groups + kBulkWarps - 1) / kBulkWarps;
         const uint64_t per_sm = stride <= 768 ? 2 : 1;  // two CTAs per SM while their slots fit
         if (grid > 148ull * per_sm) grid = 148ull * per_sm;
-        swapin_bulk_kernel<<<static_cast<uint32_t>(grid), kBulkWarps * 32, smem, static_cast<cudaStream_t>(stream)>>>(
-            static_cast<const uint8_t*>(host_pool), pool_rows, row_bytes, host_pitch, record_addr, key_space, query,
-            slot, install_mask, query_count, static_cast<uint8_t*>(slot_pool), slot_count, req_num, status, stride);
-        return asu_launch_status();
+        return launch_pdl(swapin_bulk_kernel, dim3(static_cast<uint32_t>(grid)), dim3(kBulkWarps * 32), smem,
+                          static_cast<cudaStream_t>(stream), static_cast<const uint8_t*>(host_pool), pool_rows,
+                          row_bytes, host_pitch, record_addr, key_space, query, slot, install_mask, query_count,
+                          static_cast<uint8_t*>(slot_pool), slot_count, req_num, status, stride);
     }
     uint64_t grid = (groups + kWarps - 1) / kWarps;
     if (grid > 148ull * 8ull) grid = 148ull * 8ull;
-    swapin_kernel<<<static_cast<uint32_t>(grid), kWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const int4*>(host_pool), pool_rows, row_bytes / 16, host_pitch / 16, record_addr, key_space,
-        query, slot, install_mask, query_count, static_cast<int4*>(slot_pool), slot_count, req_num, status);
-    return asu_launch_status();
+    return launch_pdl(swapin_kernel, dim3(static_cast<uint32_t>(grid)), dim3(kWarps * 32), 0,
+                      static_cast<cudaStream_t>(stream), static_cast<const int4*>(host_pool), pool_rows,
+                      row_bytes / 16, host_pitch / 16, record_addr, key_space, query, slot, install_mask, query_count,
+                      static_cast<int4*>(slot_pool), slot_count, req_num, status);
 }
 
 extern "C" int asu_host_pool_alloc(uint64_t bytes, void** host_ptr, void** device_ptr) {
