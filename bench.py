@@ -762,6 +762,7 @@ def run_decode(args, world: int, rank: int, local_rank: int):
     topk_host = torch.from_numpy(trace).pin_memory()
     topk_buf = torch.empty((L, 1, 1, DECODE_TOPK), dtype=torch.int32, device=dev)
     out_host = torch.empty((L, 1, 1, DECODE_TOPK), dtype=torch.int32, pin_memory=True)
+    out_dev = torch.empty((L, 1, 1, DECODE_TOPK), dtype=torch.int32, device=dev)
     op = torch.ops._C_ascend.npu_asu_resolve_kv_slots_single_req
 
     def resolve_layer(layer, topk, seq):
@@ -818,8 +819,8 @@ def run_decode(args, world: int, rank: int, local_rank: int):
         a.record()
         topk_buf.copy_(topk_host[step].reshape(L, 1, 1, -1), non_blocking=True)
         outs = [resolve_layer(layer, topk_buf[layer], seq) for layer in range(L)]
-        for layer in range(L):
-            out_host[layer].copy_(outs[layer], non_blocking=True)
+        torch.stack(outs, out=out_dev)  # the step's resolved slots go back in one copy
+        out_host.copy_(out_dev, non_blocking=True)
         b.record()
         b.synchronize()
         ms_e2e.append(a.elapsed_time(b))
