@@ -112,7 +112,7 @@ swapin_kernel(const int4* host, int64_t pool_rows, uint32_t cpr, uint32_t pitch1
 // flight into the slot, and the lane stops.
 constexpr int kBulkWarps = 4;
 constexpr uint32_t kBulkMaxRow = 1024;
-constexpr int kBulkSpinLimit = 1 << 20;
+constexpr int kBulkSpinLimit = 1 << 18;  // ~1 s of try_wait on B200 (each try suspends ~4 us)
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -190,6 +190,20 @@ swapin_bulk_kernel(const uint8_t* host, int64_t pool_rows, uint32_t row_bytes, u
         asm volatile("cp.async.bulk.commit_group;" ::: "memory");
     }
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // every store done before the CTA exits
+}
+
+// Self-test of the swap-in's bounded wait (mbar_wait): one thread waits on an mbarrier with an
+// arrival count of one.  With `arrive` 0 nothing arrives -- the flag that nothing sets --, the
+// wait gives up after kBulkSpinLimit tries and the kernel reports ASU_ST_TIMEOUT in status[0],
+// the path a bulk copy that never completes would take; with `arrive` 1 the thread arrives first
+// and the wait succeeds.  No copy is in flight either way, so the kernel returns normally.
+__global__ void __launch_bounds__(32) wait_selftest_kernel(int32_t arrive, int32_t* status) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    const uint32_t b = smem_addr(&bar);
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(b) : "memory");
+    if (arrive) asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" ::"r"(b) : "memory");
+    if (!mbar_wait(b, 0)) flag_status(status, 0, ASU_ST_TIMEOUT);
 }
 
 }  // namespace
@@ -298,4 +312,10 @@ extern "C" int asu_host_device_pointer(const void* host_ptr, void** device_ptr) 
     }
     *device_ptr = d;
     return ASU_OK;
+}
+
+extern "C" int asu_selftest_bounded_wait(void* stream, int32_t arrive, int32_t* status) {
+    if (!status) return ASU_ERR_ARG;
+    wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(arrive != 0, status);
+    return asu_launch_status();
 }

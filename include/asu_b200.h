@@ -212,6 +212,14 @@ int asu_host_pool_free(void* host_ptr);
  * Used to let kernels read their inputs from and write their outputs to host buffers directly. */
 int asu_host_device_pointer(const void* host_ptr, void** device_ptr);
 
+/* Self-test of the bounded device wait that asu_swapin_gather's TMA copies use (no reference
+ * counterpart).  One thread waits on an mbarrier with an arrival count of one: arrive == 0 gives
+ * a barrier nothing arrives at, so the wait runs out and ASU_ST_TIMEOUT is OR-ed
+ * into status[0] (after ~1 s on B200: 2^18 tries); arrive != 0 arrives first and leaves
+ * status[0] unchanged.  Asynchronous on
+ * `stream`; the kernel returns either way and the context stays usable. */
+int asu_selftest_bounded_wait(void* stream, int32_t arrive, int32_t* status);
+
 /* ======================================================================
  * single-request KV resolver (patch 0001 asu_kv_resolver custom op)
  * ==================================================================== */
