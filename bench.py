@@ -555,6 +555,8 @@ def run_lru1(args, world: int, rank: int, local_rank: int):
     for i in range(base):
         pools.step(q[i])
     ms = []
+    clocks = ClockSampler(gpu_index(local_rank))
+    clocks.start()
     rank_sync(torch)
     for k in range(args.steps):
         flush()
@@ -566,6 +568,7 @@ def run_lru1(args, world: int, rank: int, local_rank: int):
         b.synchronize()
         ms.append(a.elapsed_time(b))
     rank_sync(torch)
+    clock_info = clocks.stop()
     pools.check_status()
     (tot_ms,) = max_over_ranks([sum(ms)], dev)
     cpu = c_oracle.LruPools(1, 131072, 16384, 2048)
@@ -585,7 +588,7 @@ def run_lru1(args, world: int, rank: int, local_rank: int):
                      "gpu_launches": args.steps,
                      "cpu_baseline": {"value": 2048 * args.steps / cpu_s, "unit": UNIT, "cores": 1, "kind": "port",
                                       "sample": f"the same {args.steps} steps, C restatement, one thread"},
-                     "e2e": None})
+                     "e2e": None, "clocks": clock_info})
         print(json.dumps(line), flush=True)
 
 
@@ -618,6 +621,8 @@ def run_lookup(args, world: int, rank: int, local_rank: int):
     # e2e: the public API with host buffers -- the kernel reads the pinned queries and writes the
     # pinned results itself, so the bytes cross the host link inside the one launch
     H.lookup(tt, q_host, out=out_host, hit=hit_host)
+    clocks = ClockSampler(gpu_index(local_rank))
+    clocks.start()
     rank_sync(torch)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for k in range(args.steps):
@@ -636,6 +641,7 @@ def run_lookup(args, world: int, rank: int, local_rank: int):
         b.synchronize()
         ms_e2e.append(a.elapsed_time(b))
     rank_sync(torch)
+    clock_info = clocks.stop()
     exp, _ = O.gather_lookup(table, query)
     if not (out.cpu().numpy() == exp).all() or not (out_host.numpy() == exp).all():
         raise RuntimeError("lookup output differs from the oracle")
@@ -668,7 +674,8 @@ def run_lookup(args, world: int, rank: int, local_rank: int):
                                      "written to pinned host memory by the kernel (zero-copy), one launch"},
                      "gpu_launches": args.steps,
                      "cpu_baseline": {"value": n / cpu_s, "unit": UNIT, "cores": 1, "kind": "port",
-                                      "sample": "numpy restatement of the reference gather, same 64 x 2048 batch"}})
+                                      "sample": "numpy restatement of the reference gather, same 64 x 2048 batch"},
+                     "clocks": clock_info})
         print(json.dumps(line), flush=True)
 
 
@@ -1039,6 +1046,8 @@ def run_ops(args, world: int, rank: int, local_rank: int):
         return ms
 
     sweep, head = {}, None
+    clocks = ClockSampler(gpu_index(local_rank))
+    clocks.start()
     for req in OPS_REQS:
         for pattern in ("hit", "miss", "mixed"):
             case = [torch.from_numpy(x).to(dev) for x in make_index_case(req, pattern)]
@@ -1135,6 +1144,7 @@ def run_ops(args, world: int, rank: int, local_rank: int):
         if i >= args.warmup:
             e2e.append(a.elapsed_time(b))
     rank_sync(torch)
+    clock_info = clocks.stop()
     p50, p50_e2e = statistics.median(ms), statistics.median(e2e)
     p50, p50_e2e = max_over_ranks([p50, p50_e2e], dev)
     if rank != 0:
@@ -1178,6 +1188,7 @@ def run_ops(args, world: int, rank: int, local_rank: int):
                  "e2e": {"value": world * n / (p50_e2e * 1e-3), "unit": UNIT, "h2d_bytes_per_step": n * 4,
                          "d2h_bytes_per_step": n * 4},
                  "gpu_launches": iters,
+                 "clocks": clock_info,
                  "cpu_baseline": None if not cpu_n else {
                      "value": cpu_n / cpu_s, "unit": UNIT, "cores": 1, "kind": "port",
                      "sample": "C restatement of the reference lookup on the same 8-request case, state restored "
