@@ -231,7 +231,10 @@ int asu_selftest_bounded_wait(void* stream, int32_t arrive, int32_t* status);
  * TAIL_HBM -> pop free_slot_stack[--free_slot_count], copy the KV row pair from source row
  * (asu_record_addr[tok], or block_table[tok/block_size]*block_size + tok%block_size) to the
  * popped managed slot, then mark resident.  kv rows are raw bytes (kv*_row_bytes each,
- * kv0_row_bytes + kv1_row_bytes <= 1 MiB).  On return `workspace` holds the install list:
+ * kv0_row_bytes + kv1_row_bytes <= 1 MiB; row pairs of up to 1280 bytes with 16-byte-aligned
+ * starts are copied by the resolve launch itself, larger ones by a second launch).  The resolve
+ * launch is a programmatic dependent launch: stream order holds for everything it reads and
+ * writes.  On return `workspace` holds the install list:
  * int32 count, then (source row, managed slot) pairs in install order.
  * `workspace` must hold asu_kv_resolver_workspace_bytes(topk_numel) bytes of device memory.
  * status: one int32 (nullable). */
