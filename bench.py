@@ -231,12 +231,16 @@ def fold_layers(trace: np.ndarray, keys: int) -> np.ndarray:
 
 # ------------------------------------------------------------------ CPU side
 
+CPU_CYCLE_STEPS = 32  # distinct top-k sets the CPU legs cycle through (fewer would repeat into hits)
+
+
 def cpu_port_run(cfg: ResolverCfg, req: int, trace: np.ndarray, prefill: int, timed: int, time_cap_s: float,
                  threads: int):
     """The C restatement of LRUManagedCache + the row copy on `threads` host cores.
 
-    Returns (indices/s, layer-steps done, seconds).  The timed top-k sets are replayed in a
-    cycle until about time_cap_s of CPU work has been done.
+    Returns (indices/s, layer-steps done, seconds, miss rate).  The `timed` top-k sets after the
+    prefill are replayed in a cycle until about time_cap_s of CPU work has been done; the cycle
+    should be long (CPU_CYCLE_STEPS or more), or the sets repeat soon enough to become hits.
     """
     from asu_ascend_b200.workloads import record_addresses
     from oracle import c_oracle
@@ -254,6 +258,7 @@ def cpu_port_run(cfg: ResolverCfg, req: int, trace: np.ndarray, prefill: int, ti
             pools.step_all(folded[i, layer], threads=threads, want_outputs=False, host_pool=host, record=rec,
                            slot_pool=slot_pool)
     done, t_total = 0, 0.0
+    stats0 = pools.stats.sum(0).copy()
     while t_total < time_cap_s and done < 200000:
         i = prefill + (done // cfg.layers) % timed
         layer = done % cfg.layers
@@ -262,8 +267,9 @@ def cpu_port_run(cfg: ResolverCfg, req: int, trace: np.ndarray, prefill: int, ti
                        slot_pool=slot_pool)
         t_total += time.perf_counter() - t0
         done += 1
+    d = pools.stats.sum(0) - stats0  # hits, misses, installs, shortages, evictions
     pools.close()
-    return done * req * cfg.topk / t_total, done, t_total
+    return done * req * cfg.topk / t_total, done, t_total, float(d[1]) / max(1, int(d[0] + d[1]))
 
 
 def run_reference(args, world: int, rank: int):
@@ -273,16 +279,18 @@ def run_reference(args, world: int, rank: int):
     threads = len(os.sched_getaffinity(0)) or 1
     cfg = RESOLVER_WORKLOADS["resolver"]
     base = args.prefill + args.warmup
-    trace = make_trace(cfg, cfg.req, args.seed, base + args.steps)
-    value, done, secs = cpu_port_run(cfg, cfg.req, trace, base, args.steps, args.cpu_sample_s, threads)
+    cycle = max(args.steps, CPU_CYCLE_STEPS)
+    trace = make_trace(cfg, cfg.req, args.seed, base + cycle)
+    value, done, secs, miss = cpu_port_run(cfg, cfg.req, trace, base, cycle, args.cpu_sample_s, threads)
     line = base_line(world, args.steps, args.warmup, secs / done * 1e3, value,
                      {"workload": cfg.describe(), "requests_per_gpu": cfg.req, "topk": cfg.topk,
                       "context": cfg.keys, "slots_per_request": cfg.slots, "row_bytes": cfg.row})
     line.update({"impl": "reference", "cpu_steps_timed": done,
                  "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                                   "sample": f"{done} steps x {cfg.req} requests x top-k {cfg.topk} ({secs:.1f} s, "
-                                            f"cycling the {args.steps} timed top-k sets after {base} untimed steps), "
-                                            "C restatement of LRUManagedCache + row memcpy, all host threads"},
+                                            f"cycling {cycle} top-k sets of the workload after {base} untimed "
+                                            f"steps; CPU miss rate {miss:.3f}), C restatement of LRUManagedCache + "
+                                            "row memcpy, all host threads"},
                  "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
     print(json.dumps(line), flush=True)
 
@@ -369,7 +377,8 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
         r0, R = rank * cfg.req, cfg.req
     K_steps, W, L = args.steps, args.warmup, cfg.layers
     base = args.prefill + W
-    n_steps = base + 2 * K_steps
+    cpu_leg = world == 1 and not args.no_cpu_baseline and cfg.name == "resolver"
+    n_steps = base + (max(2 * K_steps, CPU_CYCLE_STEPS) if cpu_leg else 2 * K_steps)
     trace = make_trace(cfg, R, args.seed + 1000 * (r0 + 1), n_steps)
     q_dev = torch.from_numpy(trace).to(dev)
     q_host = torch.from_numpy(trace).pin_memory()
@@ -477,14 +486,15 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
         achieved = alg_bytes / (sum(resolve_ms) * 1e-3) / 1e9
         swap_gbs = installs * cfg.row / (sum(swapin_ms) * 1e-3) / 1e9
         cpu = None
-        if world == 1 and not args.no_cpu_baseline and cfg.name == "resolver":
+        if cpu_leg:
             os.sched_setaffinity(0, all_cpus)  # the CPU leg uses every host thread again
             threads = len(all_cpus)
-            v, done, secs = cpu_port_run(cfg, R, trace, base, K_steps, args.cpu_sample_s, threads)
+            cycle = trace.shape[0] - base
+            v, done, secs, miss = cpu_port_run(cfg, R, trace, base, cycle, args.cpu_sample_s, threads)
             cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                   "sample": f"{done} steps x {R} requests x top-k {cfg.topk} ({secs:.1f} s, cycling the "
-                             f"{K_steps} timed top-k sets of this workload), C restatement of LRUManagedCache + "
-                             "row memcpy, all host threads"}
+                   "sample": f"{done} steps x {R} requests x top-k {cfg.topk} ({secs:.1f} s, cycling {cycle} "
+                             f"top-k sets of this workload; CPU miss rate {miss:.3f}), C restatement of "
+                             "LRUManagedCache + row memcpy, all host threads"}
         config = {"workload": cfg.describe(), "requests_per_gpu": R, "global_batch": job_req, "topk": cfg.topk,
                   "layers": L, "context": cfg.keys, "slots_per_request": cfg.slots, "free_target": cfg.target,
                   "row_bytes": cfg.row,
