@@ -483,6 +483,61 @@ def test_lru_kernel_shapes_against_oracle(S, Q):
     _lru_run_and_compare(pools, oracle, steps, check_state_every=3)
 
 
+def test_lru_stress_shape_against_oracle():
+    """The stress configuration's shape -- a 1M-token key space, 8192 slots, target 2048, uniform
+    top-k 2048 with 20% reuse (~80% misses) -- on 8 requests, full state against the oracle."""
+    from asu_ascend_b200.lru import LruSlotPools
+    from asu_ascend_b200.workloads import FastLocalityTrace
+
+    R, K = 8, 1 << 20
+    tr = FastLocalityTrace(R, K, topk=2048, reuse=0.2, zipf_s=None, seed=77)
+    steps = [tr.step() for _ in range(6)]
+    pools = LruSlotPools(R, K, 8192, 2048, 2048, device=DEV)
+    oracle = [O.LruPool(8192, 2048) for _ in range(R)]
+    _lru_run_and_compare(pools, oracle, steps, check_state_every=5)
+
+
+def test_lru_full_stress_size_invariants():
+    """The full stress size (128 requests, 1M-token key space): after every step the two maps are
+    inverse to each other, the order row lists exactly the resident slots, the free stack the
+    others, and each request's installs went to distinct slots -- properties that do not need
+    an oracle run at this size."""
+    from asu_ascend_b200.lru import LruSlotPools
+    from asu_ascend_b200.workloads import FastLocalityTrace
+
+    R, K, S = 128, 1 << 20, 8192
+    tr = FastLocalityTrace(R, K, topk=2048, reuse=0.2, zipf_s=None, seed=78)
+    pools = LruSlotPools(R, K, S, 2048, 2048, device=DEV)
+    ar = torch.arange(S, device=DEV)
+    for _ in range(4):
+        q = T(tr.step())
+        out = pools.step(q)
+        free = pools.free_count.long()
+        s2t = pools.slot_to_token
+        resident = s2t >= 0
+        assert torch.equal(resident.sum(1), S - free)
+        rows, slots = torch.nonzero(resident, as_tuple=True)
+        assert torch.equal(pools.token_to_slot[rows, s2t[rows, slots].long()], slots.int())
+        assert int((pools.token_to_slot >= 0).sum()) == int(resident.sum())
+        order_ok = ar[None, :] < (S - free)[:, None]
+        ordered = torch.where(order_ok, pools.lru_order, torch.full_like(pools.lru_order, -1))
+        assert torch.equal(torch.sort(ordered, 1).values[:, -1].ge(0), (S - free) > 0)
+        marks = torch.zeros((R, S), dtype=torch.int32, device=DEV)
+        marks.scatter_add_(1, ordered.clamp(min=0).long(), order_ok.int())
+        assert torch.equal(marks > 0, resident) and int(marks.max()) <= 1
+        stack_ok = ar[None, :] < free[:, None]
+        fmarks = torch.zeros((R, S), dtype=torch.int32, device=DEV)
+        fmarks.scatter_add_(1, pools.free_stack.clamp(min=0).long(), stack_ok.int())
+        assert torch.equal(fmarks > 0, ~resident) and int(fmarks.max()) <= 1
+        inst = out.install
+        islots = torch.where(inst, out.slot, torch.full_like(out.slot, -1))
+        imarks = torch.zeros((R, S), dtype=torch.int32, device=DEV)
+        imarks.scatter_add_(1, islots.clamp(min=0).long(), inst.int())
+        assert int(imarks.max()) <= 1
+        assert bool((out.slot[out.hit | out.install] >= 0).all())
+    pools.check_status()
+
+
 def test_lru_c2_shape_against_oracle():
     """128 requests, 128K keys, 8192 slots, target 2048, top-k 2048 with c0 locality: 6 steps."""
     from asu_ascend_b200.lru import LruSlotPools
