@@ -595,6 +595,46 @@ def test_swapin_bytes_exact(row_bytes, R, S, Q):
     pool.close()
 
 
+def test_swapin_full_resolver_workload_bytes():
+    """The default benchmark configuration at full size -- 128 requests, 131072 tokens, 8192
+    slots, top-k 2048 with reuse + Zipf locality, 656-byte rows in a 2^20-row pinned pool at the
+    768-byte pitch: after each of four steps every row installed in that step equals its host
+    record byte for byte, and so does a sample of every request's resident rows."""
+    from asu_ascend_b200.host_pool import HostRowPool, check_status
+    from asu_ascend_b200.lru import LruSlotPools
+    from asu_ascend_b200.workloads import LocalityTrace, record_addresses_torch
+
+    R, K, S, Q, row = 128, 131072, 8192, 2048, 656
+    pool = HostRowPool(rows=1 << 20, row_bytes=row)
+    pool.fill_random(13)
+    host = pool.tensor  # CPU view of the pinned rows
+    rec = record_addresses_torch(R, K, pool.rows, DEV)
+    tr = LocalityTrace(R, K, topk=Q, seed=15)
+    lru = LruSlotPools(R, K, S, 2048, Q, device=DEV)
+    kv = torch.zeros((R, S, row), dtype=torch.uint8, device=DEV)
+    status = torch.zeros(R, dtype=torch.int32, device=DEV)
+    g = torch.Generator().manual_seed(3)
+    for _ in range(4):
+        q = T(tr.step())
+        out = lru.step(q)
+        pool.swapin(rec, q, out.slot, out.install, kv, status=status)
+        torch.cuda.synchronize()
+        r_i, p_i = torch.nonzero(out.install, as_tuple=True)
+        src = rec[r_i, q[r_i, p_i].long()].long()
+        assert r_i.numel() > 0
+        np.testing.assert_array_equal(N(kv[r_i, out.slot[r_i, p_i].long()]), host[src.cpu()].numpy())
+        # a sample of resident rows of every request: slot s holds the record of slot_to_token[r, s]
+        s_pick = torch.randint(0, S, (R, 64), generator=g).to(DEV)
+        tok = lru.slot_to_token.gather(1, s_pick)
+        ok = tok >= 0
+        rr = torch.arange(R, device=DEV)[:, None].expand(R, 64)[ok]
+        srcs = rec[rr, tok[ok].long()].long()
+        np.testing.assert_array_equal(N(kv[rr, s_pick[ok]]), host[srcs.cpu()].numpy())
+    check_status(status, "swapin")
+    lru.check_status()
+    pool.close()
+
+
 @pytest.mark.parametrize("row_bytes,pitch", [(656, None), (656, 656), (64, None), (1024, None), (2048, None)])
 def test_swapin_direct_masks_errors_and_pitches(row_bytes, pitch):
     """The swap-in alone, on hand-made install masks: query counts that are not multiples of
