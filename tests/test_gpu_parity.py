@@ -538,6 +538,39 @@ def test_lru_full_stress_size_invariants():
     pools.check_status()
 
 
+def test_lru_multilayer_batch_of_1024_requests():
+    """The request-sharded configuration's per-GPU batch at one GPU: 1024 requests (several
+    waves of CTAs), 131072 tokens, 8192 slots, top-k 2048.  Requests 0, 511 and 1023 are checked
+    against the oracle step by step, and the state of all of them for the map invariants."""
+    from asu_ascend_b200.lru import LruSlotPools
+    from asu_ascend_b200.workloads import FastLocalityTrace
+
+    R, K, S = 1024, 131072, 8192
+    tr = FastLocalityTrace(R, K, topk=2048, seed=79)
+    pools = LruSlotPools(R, K, S, 2048, 2048, device=DEV)
+    picks = (0, 511, 1023)
+    oracle = {r: O.LruPool(S, 2048) for r in picks}
+    for _ in range(4):
+        q = tr.step()
+        out = pools.step(T(q))
+        slot, hit, inst = N(out.slot), N(out.hit), N(out.install)
+        for r in picks:
+            res = oracle[r].step(q[r])
+            np.testing.assert_array_equal(slot[r], res.slot)
+            np.testing.assert_array_equal(hit[r], res.hit)
+            np.testing.assert_array_equal(inst[r], res.install)
+    for r in picks:
+        et2s, es2t, eorder, estack, ecount = oracle[r].export_state(K)
+        assert int(N(pools.free_count)[r]) == ecount
+        np.testing.assert_array_equal(N(pools.slot_to_token[r]), es2t)
+        np.testing.assert_array_equal(N(pools.lru_order[r])[: S - ecount], eorder[: S - ecount])
+    s2t = pools.slot_to_token
+    rows, slots = torch.nonzero(s2t >= 0, as_tuple=True)
+    assert torch.equal(pools.token_to_slot[rows, s2t[rows, slots].long()], slots.int())
+    assert int((pools.token_to_slot >= 0).sum()) == rows.numel()
+    pools.check_status()
+
+
 def test_lru_c2_shape_against_oracle():
     """128 requests, 128K keys, 8192 slots, target 2048, top-k 2048 with c0 locality: 6 steps."""
     from asu_ascend_b200.lru import LruSlotPools
