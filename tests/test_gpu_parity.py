@@ -668,6 +668,38 @@ def test_swapin_full_resolver_workload_bytes():
     pool.close()
 
 
+def test_swapin_full_stress_block_bytes():
+    """The block-granular stress configuration at full size: 128 requests, 16384 blocks of 64
+    tokens, 128 block slots, top-k 32 blocks with 20% reuse, 41,984-byte block rows (the 16-byte
+    load swap-in kernel) in a 16384-row pinned pool: every block installed in each of four steps
+    equals its host record byte for byte."""
+    from asu_ascend_b200.host_pool import HostRowPool, check_status
+    from asu_ascend_b200.lru import LruSlotPools
+    from asu_ascend_b200.workloads import FastLocalityTrace, record_addresses_torch
+
+    R, K, S, Q, row = 128, 16384, 128, 32, 41984
+    pool = HostRowPool(rows=16384, row_bytes=row)
+    pool.fill_random(17)
+    host = pool.tensor
+    rec = record_addresses_torch(R, K, pool.rows, DEV)
+    tr = FastLocalityTrace(R, K, topk=Q, reuse=0.2, zipf_s=None, seed=19)
+    lru = LruSlotPools(R, K, S, Q, Q, device=DEV)
+    kv = torch.zeros((R, S, row), dtype=torch.uint8, device=DEV)
+    status = torch.zeros(R, dtype=torch.int32, device=DEV)
+    for _ in range(4):
+        q = T(tr.step())
+        out = lru.step(q)
+        pool.swapin(rec, q, out.slot, out.install, kv, status=status)
+        torch.cuda.synchronize()
+        r_i, p_i = torch.nonzero(out.install, as_tuple=True)
+        assert r_i.numel() > 0
+        src = rec[r_i, q[r_i, p_i].long()].long()
+        np.testing.assert_array_equal(N(kv[r_i, out.slot[r_i, p_i].long()]), host[src.cpu()].numpy())
+    check_status(status, "swapin")
+    lru.check_status()
+    pool.close()
+
+
 @pytest.mark.parametrize("row_bytes,pitch", [(656, None), (656, 656), (64, None), (1024, None), (2048, None)])
 def test_swapin_direct_masks_errors_and_pitches(row_bytes, pitch):
     """The swap-in alone, on hand-made install masks: query counts that are not multiples of
