@@ -136,3 +136,59 @@ def test_managed_rows_equal_original_rows_decode_case():
     again = resolve()
     assert int(ctx.free_slot_count.item()) == left
     assert torch.equal(again, slots)
+
+
+def test_decode_flow_at_full_context_against_oracle():
+    """The decode workload's size: a 131072-token context with 130944 ASU-managed prefix tokens and
+    a paged tail, the manager's default managed slot count (one per context position), bf16 rows
+    of 512 + 64 elements, a 2048-entry top-k with step-to-step reuse and the newest token always
+    included; three decode steps, state arrays, slots and every managed row exact."""
+    import asu_ascend_b200
+
+    asu_ascend_b200.load()
+    from asu_ascend_b200 import manager as M
+
+    rng = np.random.Generator(np.random.PCG64(21))
+    max_seq, bs = 131072, 64
+    actual, prefix = 131000, 130944
+    nblk = max_seq // bs
+    bt = rng.permutation(nblk + 16)[:nblk].astype(np.int32)
+    kv0 = torch.randn(nblk + 16, bs, 1, 512, device=DEV).to(torch.bfloat16)
+    kv1 = torch.randn(nblk + 16, bs, 1, 64, device=DEV).to(torch.bfloat16)
+    mgr = M.ASUFullKVCacheManagerFunctional.from_kv_caches({"l": (kv0, kv1)}, max_seq, bs, enabled=True)
+    ctx = mgr.get_layer_context("l")
+    ctx.managed_kv_cache_0.zero_()
+    ctx.managed_kv_cache_1.zero_()
+    mgr.reset_single_request("r", actual, prefix, torch.from_numpy(bt[None, :]))
+    o0, o1 = ctx.original_kv_cache_views((kv0, kv1))
+    slots = ctx.managed_slot_count
+    ts, rec, hs, own, stack, cnt = O.reset_state(max_seq, slots, bs, actual, prefix, bt)
+    u16 = lambda t: t.view(torch.int16).cpu().numpy().view(np.uint16)  # noqa: E731
+    s0, s1 = u16(o0), u16(o1)
+    e0 = np.zeros((slots,) + s0.shape[1:], np.uint16)
+    e1 = np.zeros((slots,) + s1.shape[1:], np.uint16)
+    seq = actual
+    prev = rng.choice(seq, 2048, replace=False)
+    for step in range(3):
+        keep = rng.choice(prev, 1434, replace=False)
+        fresh = rng.integers(0, seq, 2048 - keep.size)
+        topk = np.concatenate([keep, fresh]).astype(np.int32)[None, None, :]
+        topk[0, 0, -1] = seq - 1
+        prev = topk.reshape(-1)
+        out = torch.ops._C_ascend.npu_asu_resolve_kv_slots_single_req(
+            torch.from_numpy(topk).to(DEV), ctx.actual_seq_len, ctx.managed_prefix_len, ctx.token_state,
+            ctx.asu_record_addr, ctx.hbm_slot_of_token, ctx.slot_owner_token, ctx.free_slot_stack,
+            ctx.free_slot_count, torch.from_numpy(bt[None, :]).to(DEV), o0, o1, ctx.managed_kv_cache_0,
+            ctx.managed_kv_cache_1, bs)
+        exp = O.resolve_kv_slots_single_req(topk, seq, ts, rec, hs, own, stack, cnt, bt, s0, s1, e0, e1, bs)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.cpu().numpy(), exp)
+        np.testing.assert_array_equal(ctx.token_state.cpu().numpy(), ts)
+        np.testing.assert_array_equal(ctx.hbm_slot_of_token.cpu().numpy(), hs)
+        np.testing.assert_array_equal(ctx.slot_owner_token.cpu().numpy(), own)
+        assert int(ctx.free_slot_count.item()) == int(cnt[0])
+        np.testing.assert_array_equal(u16(ctx.managed_kv_cache_0), e0)
+        np.testing.assert_array_equal(u16(ctx.managed_kv_cache_1), e1)
+        mgr.mark_decode_token(seq)
+        ts[seq] = O.TAIL_HBM
+        seq += 1
