@@ -77,3 +77,26 @@ def test_producer_write_back_then_swap_in_round_trip():
         got = slot_pool[0, out.slot[0].long()]
         assert torch.equal(got, prefill[1][q[0].long()])
     pool.close()
+
+
+def test_writeback_full_prefill_size():
+    """The write-back workload's size: a 128K-token prefill of 656-byte rows for each of 4 layers,
+    written into consecutive extents of a pinned pool under their MicroKV keys; every row of
+    every layer reads back unchanged (the whole pool, not a sample)."""
+    from asu_ascend_b200 import kv_store as KV
+    from asu_ascend_b200.host_pool import HostRowPool
+
+    tokens, row, layers = 131072, 656, 4
+    pool = HostRowPool(rows=layers * tokens, row_bytes=row)
+    store = KV.HostKVStore(pool.array, tokens_per_extent=tokens, pool=pool)
+    g = torch.Generator(device=DEV).manual_seed(8)
+    src = [torch.randint(0, 256, (tokens, row), dtype=torch.uint8, device=DEV, generator=g) for _ in range(layers)]
+    for layer in range(layers):
+        store.write_back(KV.KV_MLA_TOKEN, "prefill-full", layer, 0, src[layer])
+    torch.cuda.synchronize()
+    for layer in range(layers):
+        base = store.extent_base(KV.KV_MLA_TOKEN, "prefill-full", layer)
+        np.testing.assert_array_equal(pool.array[base:base + tokens], src[layer].cpu().numpy())
+    for t in (0, 65535, tokens - 1):
+        assert store.get(KV.KV_MLA_TOKEN, KV.make_key("prefill-full", 3, t)) == src[3][t].cpu().numpy().tobytes()
+    pool.close()
