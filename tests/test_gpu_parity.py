@@ -363,6 +363,32 @@ def test_batch_lru_random_states_against_oracle(S, Q, R):
             np.testing.assert_array_equal(N(tl)[r].astype(np.int32), state[r][2])
 
 
+def test_batch_lru_reference_benchmark_case_64_requests():
+    """The SIMT harness's benchmark case at its largest batch: 64 requests, every one of the 10240
+    slots resident, 1536 hits and 512 misses of 2048 per request, two rounds (the second on the
+    state the first left); every request's outputs and state against the oracle."""
+    from asu_ascend_b200.workloads import simt_case
+
+    t2s, s2t, lru, q = simt_case(64, 1536, seed=64)
+    tt, ts, tl = T(t2s), T(s2t), T(lru)
+    state = [[t2s[r].tolist(), s2t[r].tolist(), lru[r].astype(np.int32).tolist()] for r in range(64)]
+    rng = np.random.Generator(np.random.PCG64(65))
+    for rnd in range(2):
+        if rnd:  # second round: half of the first round's ids again, half fresh
+            q = np.stack([np.concatenate([rng.choice(q[r], 1024, replace=False),
+                                          rng.choice(131072, 1024, replace=False)]).astype(np.int32)
+                          for r in range(64)])
+        sid, mask = torch.ops.asu.asu_hbm_index_lookup_simt(tt, ts, tl, T(q), 64)
+        for r in range(64):
+            es, em = O.batch_lru(q[r].tolist(), *state[r])
+            np.testing.assert_array_equal(N(sid)[r], es)
+            np.testing.assert_array_equal(N(mask)[r], em)
+        np.testing.assert_array_equal(N(ts), np.asarray([st[1] for st in state], np.int32))
+        np.testing.assert_array_equal(N(tl).astype(np.int32), np.asarray([st[2] for st in state], np.int32))
+        for r in (0, 31, 63):
+            np.testing.assert_array_equal(N(tt)[r], state[r][0])
+
+
 def test_batch_lru_no_victim_leaves_state_unchanged():
     t2s, s2t, lru = _simt_state([0, 1, 2, 3])
     tt, ts, tl = T(t2s), T(s2t), T(lru)
