@@ -105,6 +105,29 @@ def test_lookup_only_workload_full_size():
     assert 0.8 < exp_hit.mean() < 0.9
 
 
+@pytest.mark.parametrize("pct,dups", [(5, False), (100, False), (100, True)])
+def test_lookup_random_update_full_size(pct, dups):
+    """The gather + seeded random update on the lookup workload's full size (64 x 128K tables,
+    64 x 2048 queries): the gathered values and the whole updated table against the oracle, at
+    the benchmark's 5%, at 100% (every query position updated), and at 100% with duplicate query
+    keys, where the last writer in update order must win."""
+    from asu_ascend_b200 import hbm_lookup_update as H
+    from asu_ascend_b200.workloads import lookup_only_case
+
+    table, query = lookup_only_case()
+    if dups:
+        query = query.copy()
+        query[:, 1::2] = query[:, 0::2]  # every key twice
+    rng = np.random.Generator(np.random.PCG64(pct))
+    new = rng.integers(0, 1 << 20, query.shape, dtype=np.int32)
+    states = T(table)
+    out = H.lookup_random_update(torch.zeros_like(states), states, T(query), T(new), seed=2026,
+                                 update_percent=pct)
+    exp_out, _ = O.gather_lookup(table, query)
+    np.testing.assert_array_equal(N(out).reshape(exp_out.shape), exp_out)
+    np.testing.assert_array_equal(N(states), O.random_update(table, query, new, 2026, pct))
+
+
 def test_lookup_zero_copy_host_buffers():
     """Queries read from, results written to pinned host memory by the kernel itself."""
     from asu_ascend_b200 import hbm_lookup_update as H
