@@ -144,18 +144,44 @@ L2_NOTE = "flushed before every timed step (256 MiB write, then 256 MiB read so 
 # ------------------------------------------------------------------ clocks
 
 class ClockSampler:
-    """nvidia-smi samples every 200 ms while the timed region runs."""
+    """SM clocks and clock-event (throttle) reasons while the timed region runs.
+
+    NVML is polled every 20 ms on a thread, with one sample taken at start(), so a timed region
+    shorter than the polling interval still has its clocks recorded; where NVML is unavailable,
+    nvidia-smi samples every 200 ms instead."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # (name in the JSON line, NVML constant, its value in nvml.h)
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown", 0x8),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap", 0x4))
 
     def __init__(self, gpu_index: int):
         self.gpu_index = gpu_index
         self.lines: list[str] = []
         self.proc = None
+        self.nvml = None
+        self.samples: list[tuple[int, int, int]] = []
+        self._done = threading.Event()
+        self._thread = None
 
     def start(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.gpu_index)
+            self.nvml = pynvml
+            self._sample()
+            self._thread = threading.Thread(target=self._poll, daemon=True)
+            self._thread.start()
+            return
+        except Exception:
+            self.nvml = None
+            self.samples = []
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
                                           "-lms", "200", "-i", str(self.gpu_index)],
@@ -164,11 +190,33 @@ class ClockSampler:
         except Exception:
             self.proc = None
 
+    def _sample(self):
+        n = self.nvml
+        sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+        mx = n.nvmlDeviceGetMaxClockInfo(self.handle, n.NVML_CLOCK_SM)
+        get = getattr(n, "nvmlDeviceGetCurrentClocksEventReasons", None) or n.nvmlDeviceGetCurrentClocksThrottleReasons
+        self.samples.append((sm, mx, get(self.handle)))
+
+    def _poll(self):
+        while not self._done.wait(0.02):
+            try:
+                self._sample()
+            except Exception:
+                return
+
     def _read(self):
         for ln in self.proc.stdout:
             self.lines.append(ln.strip())
 
     def stop(self) -> dict:
+        if self.nvml is not None:
+            self._done.set()
+            self._thread.join(timeout=2)
+            reasons = {name for name, const, bit in self.REASONS
+                       if any(r & getattr(self.nvml, const, bit) for _, _, r in self.samples)}
+            sm = [s for s, _, _ in self.samples]
+            return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(m for _, m, _ in self.samples),
+                    "reasons": sorted(reasons), "samples": len(sm), "source": "NVML every 20 ms"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         time.sleep(0.25)
@@ -192,7 +240,7 @@ class ClockSampler:
                 if v.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi every 200 ms"}
 
 
 def gpu_index(local_rank: int) -> int:

@@ -32,3 +32,33 @@ def test_reference_arm_prints_one_contract_line():
     cb = a["cpu_baseline"]
     assert cb["value"] == a["value"] and cb["kind"] == "port" and cb["cores"] >= 1 and cb["sample"]
     assert a["e2e"] == {"value": a["value"], "unit": a["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_clock_sampler_reads_nvml_and_maps_event_reasons(monkeypatch):
+    """The clock sampler on a fake NVML: a sample at start and polls while running, the median SM
+    clock, the maximum, and the throttle reasons seen in any sample (power cap here)."""
+    import time
+    import types
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    clocks = iter([1965, 1965, 1800] + [1965] * 1000)
+    fake = types.SimpleNamespace(
+        NVML_CLOCK_SM=1, nvmlClocksEventReasonSwPowerCap=0x4, nvmlClocksEventReasonHwSlowdown=0x8,
+        nvmlInit=lambda: None, nvmlDeviceGetHandleByIndex=lambda i: ("gpu", i),
+        nvmlDeviceGetClockInfo=lambda h, c: next(clocks), nvmlDeviceGetMaxClockInfo=lambda h, c: 1965,
+        nvmlDeviceGetCurrentClocksEventReasons=lambda h: 0x4)
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    c = bench.ClockSampler(3)
+    c.start()
+    time.sleep(0.1)
+    out = c.stop()
+    assert out["samples"] >= 2 and out["sm_max_mhz"] == 1965 and out["sm_mhz"] == 1965
+    assert out["reasons"] == ["sw_power_cap"] and out["source"].startswith("NVML")
+    # a sampler whose NVML is missing falls back to nvidia-smi, or reports that it has none
+    monkeypatch.setitem(sys.modules, "pynvml", None)
+    c = bench.ClockSampler(0)
+    c.start()
+    out = c.stop()
+    assert "sm_mhz" in out and "reasons" in out
