@@ -18,9 +18,9 @@ The manager comes from ``attn_metadata.asu_kv_cache_manager`` as in the referenc
 else from the class attribute ``asu_manager``; the request id from
 ``attn_metadata.asu_req_id``, else ``"__single_req__"``::
 
-    Impl = asu_flashmla_sparse_impl()
-    Impl.asu_manager = sparse_mla.contexts_for_mla(kv_caches, max_model_len, block_size)
-    # and build Impl where vLLM builds FlashMLASparseImpl (FlashMLASparseBackend.get_impl_cls)
+    register_flashmla_sparse_override()   # before the model is built: vLLM's FLASHMLA_SPARSE
+                                          # backend then resolves to ASUFlashMLASparseBackend
+    attach_manager(sparse_mla.contexts_for_mla(kv_caches, max_model_len, block_size))
 """
 
 from __future__ import annotations
@@ -122,3 +122,45 @@ def asu_flashmla_sparse_impl():
             return self._asu_fp8_decode(q, *r, meta.decode.kernel_metadata)
 
     return ASUFlashMLASparseImpl
+
+
+@functools.lru_cache(maxsize=1)
+def asu_flashmla_sparse_backend():
+    """vLLM's FlashMLASparseBackend with ASUFlashMLASparseImpl as its implementation class; the
+    name, metadata builder, cache shape and kernel-block sizes stay vLLM's."""
+    from vllm.v1.attention.backends.mla.flashmla_sparse import FlashMLASparseBackend
+
+    impl = asu_flashmla_sparse_impl()
+
+    class ASUFlashMLASparseBackend(FlashMLASparseBackend):
+        @staticmethod
+        def get_impl_cls():
+            return impl
+
+    for cls in (ASUFlashMLASparseBackend, impl):  # importable by name (vLLM resolves class paths)
+        cls.__module__ = __name__
+        cls.__qualname__ = cls.__name__
+    return ASUFlashMLASparseBackend
+
+
+def __getattr__(name):
+    """Module attributes built on first use, so importing this module does not import vLLM."""
+    if name == "ASUFlashMLASparseBackend":
+        return asu_flashmla_sparse_backend()
+    if name == "ASUFlashMLASparseImpl":
+        return asu_flashmla_sparse_impl()
+    raise AttributeError(name)
+
+
+def register_flashmla_sparse_override() -> None:
+    """Point vLLM's FLASHMLA_SPARSE attention backend at ASUFlashMLASparseBackend (vLLM's
+    ``register_backend`` override).  Call it before vLLM builds the model; batches the ASU path
+    does not take still run vLLM's own code."""
+    from vllm.v1.attention.backends.registry import AttentionBackendEnum, register_backend
+
+    register_backend(AttentionBackendEnum.FLASHMLA_SPARSE, f"{__name__}.ASUFlashMLASparseBackend")
+
+
+def attach_manager(manager) -> None:
+    """The manager every ASUFlashMLASparseImpl uses when the attention metadata carries none."""
+    asu_flashmla_sparse_impl().asu_manager = manager

@@ -134,3 +134,25 @@ def test_subclass_routes_fp8_decode_to_the_resolver(monkeypatch):
     assert impl.forward_mqa(q, kv, _md(fp8_use_mixed_batch=False, fp8_extra_metadata=with_prefill),
                             layer)[0] == "stock-sep"
     assert len(seen) == n
+
+
+def test_registered_override_resolves_to_the_asu_backend():
+    pytest.importorskip("vllm")
+    from vllm.v1.attention.backends.mla.flashmla_sparse import FlashMLASparseBackend, FlashMLASparseImpl
+    from vllm.v1.attention.backends.registry import _ATTN_OVERRIDES, AttentionBackendEnum
+
+    before = dict(_ATTN_OVERRIDES)
+    try:
+        V.register_flashmla_sparse_override()
+        cls = AttentionBackendEnum.FLASHMLA_SPARSE.get_class()
+        assert cls is V.asu_flashmla_sparse_backend() and issubclass(cls, FlashMLASparseBackend)
+        assert cls.get_name() == FlashMLASparseBackend.get_name()
+        impl = cls.get_impl_cls()
+        assert impl is V.ASUFlashMLASparseImpl and issubclass(impl, FlashMLASparseImpl)
+        m = FakeManager()
+        V.attach_manager(m)
+        assert impl.asu_manager is m
+    finally:
+        _ATTN_OVERRIDES.clear()
+        _ATTN_OVERRIDES.update(before)
+        V.asu_flashmla_sparse_impl().asu_manager = None
