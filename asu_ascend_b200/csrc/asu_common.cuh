@@ -130,6 +130,15 @@ __device__ __forceinline__ int block_exclusive_scan_1b(int v, int* warp_sums, in
 
 }  // namespace asu
 
+// Host-side helpers shared by the entry points (defined in capi_misc.cu; thread-safe).
+// SM count of the current device, queried once per device; 1 if the query fails (the launch
+// that follows then reports the device's error itself).
+int asu_sm_count();
+// Opt-in dynamic shared-memory limit of `kernel` on the current device (the device's opt-in
+// maximum minus the kernel's static shared memory), set as the kernel's attribute once per
+// (device, kernel).  Returns ASU_OK or ASU_ERR_CUDA_BASE + cudaError_t.
+int asu_max_dynamic_smem(const void* kernel, int* max_dynamic);
+
 // Host-side launch-error helper shared by the entry points.
 static inline int asu_launch_status() {
     cudaError_t e = cudaGetLastError();

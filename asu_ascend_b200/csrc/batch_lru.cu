@@ -231,34 +231,13 @@ batch_lru_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int16_t* 
 template <int IPT_Q, int IPT_S>
 int launch_batch(cudaStream_t s, int32_t* t2s, int32_t* s2t, int16_t* lru, const int32_t* q, int32_t* slot_ids,
                  uint8_t* mask, uint32_t R, uint32_t K, uint32_t S, uint32_t Q, int32_t* status) {
-    static unsigned long long configured = 0;  // one bit per device
-    static int max_dynamic[64];
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess || dev < 0 || dev >= 64) {
-        cudaGetLastError();
-        return e != cudaSuccess ? ASU_ERR_CUDA_BASE + static_cast<int>(e) : ASU_ERR_ARG;
-    }
-    if (!((configured >> dev) & 1ull)) {
-        int optin = 0;
-        cudaFuncAttributes fa;
-        e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, batch_lru_kernel<IPT_Q, IPT_S>);
-        if (e == cudaSuccess) {
-            max_dynamic[dev] = optin - static_cast<int>(fa.sharedSizeBytes);
-            e = cudaFuncSetAttribute(batch_lru_kernel<IPT_Q, IPT_S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     max_dynamic[dev]);
-        }
-        if (e != cudaSuccess) {
-            cudaGetLastError();  // leave no error behind for the caller's runtime checks
-            return ASU_ERR_CUDA_BASE + static_cast<int>(e);
-        }
-        configured |= 1ull << dev;
-    }
+    int max_dynamic = 0;
+    const int rc = asu_max_dynamic_smem(reinterpret_cast<const void*>(batch_lru_kernel<IPT_Q, IPT_S>), &max_dynamic);
+    if (rc != ASU_OK) return rc;
     uint32_t H = 32;
     while (H < 2 * (Q ? Q : 1)) H <<= 1;
     const size_t smem = batch_smem_bytes(S, Q, H);
-    if (smem > static_cast<size_t>(max_dynamic[dev])) return ASU_ERR_ARG;
+    if (smem > static_cast<size_t>(max_dynamic)) return ASU_ERR_ARG;
     const uint32_t grid = R < 65535u ? R : 65535u;
     batch_lru_kernel<IPT_Q, IPT_S><<<grid, kThreads, smem, s>>>(t2s, s2t, lru, q, slot_ids, mask, R, K, S, Q, H,
                                                                  status);

@@ -167,7 +167,7 @@ random_update_kernel(int32_t* __restrict__ table, uint32_t index_size, const int
 
 inline uint32_t grid_for(uint64_t work, int threads) {
     uint64_t g = (work + threads - 1) / threads;
-    const uint64_t cap = 148ull * 16ull;
+    const uint64_t cap = static_cast<uint64_t>(asu_sm_count()) * 16ull;
     if (g > cap) g = cap;
     return static_cast<uint32_t>(g < 1 ? 1 : g);
 }
@@ -210,7 +210,8 @@ extern "C" int asu_random_update(void* stream, int32_t* table, uint32_t index_si
     uint64_t update_num = (static_cast<uint64_t>(query_len) * update_percent) / 100u;
     if (update_num > query_len) update_num = query_len;
     if (update_num == 0) return ASU_OK;
-    const uint32_t grid = req_num < 148u * 8u ? req_num : 148u * 8u;
+    const uint32_t cap = static_cast<uint32_t>(asu_sm_count()) * 8u;
+    const uint32_t grid = req_num < cap ? req_num : cap;
     random_update_kernel<<<grid, kUpdateThreads, 0, static_cast<cudaStream_t>(stream)>>>(
         table, index_size, query, new_states, query_len, req_num, seed, static_cast<uint32_t>(update_num), status);
     return asu_launch_status();

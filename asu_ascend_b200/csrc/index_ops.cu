@@ -225,7 +225,10 @@ ops_maintain_kernel(int32_t* __restrict__ index, int32_t* __restrict__ slot_to_i
     }
 }
 
-inline uint32_t req_grid(uint32_t req_num) { return req_num < 148u * 16u ? req_num : 148u * 16u; }
+inline uint32_t req_grid(uint32_t req_num) {
+    const uint32_t cap = static_cast<uint32_t>(asu_sm_count()) * 16u;
+    return req_num < cap ? req_num : cap;
+}
 
 }  // namespace
 }  // namespace asu

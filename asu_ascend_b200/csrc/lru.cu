@@ -418,34 +418,12 @@ int launch_lru(cudaStream_t s, int32_t* t2s, int32_t* s2t, int32_t* order, int32
                const int32_t* query, int32_t* slot_out, uint8_t* hit, uint8_t* inst, int32_t* evicted,
                uint32_t ev_stride, int32_t* ev_count, int64_t* stats, int32_t* status, uint32_t R, uint32_t K,
                uint32_t S, uint32_t Q, uint32_t target) {
-    // Per device: the opt-in shared-memory limit minus the kernel's static shared memory.
-    static unsigned long long configured = 0;
-    static int max_dynamic[64];
     int log2h = 0;
     const size_t smem = lru_smem_bytes(S, Q, &log2h);
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess || dev >= 64) {
-        cudaGetLastError();
-        return e != cudaSuccess ? ASU_ERR_CUDA_BASE + static_cast<int>(e) : ASU_ERR_ARG;
-    }
-    if (!((configured >> dev) & 1ull)) {
-        int optin = 0;
-        cudaFuncAttributes fa;
-        e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, lru_step_kernel<IPT_Q, IPT_S>);
-        if (e == cudaSuccess) {
-            max_dynamic[dev] = optin - static_cast<int>(fa.sharedSizeBytes);
-            e = cudaFuncSetAttribute(lru_step_kernel<IPT_Q, IPT_S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     max_dynamic[dev]);
-        }
-        if (e != cudaSuccess) {
-            cudaGetLastError();  // leave no error behind for the caller's runtime checks
-            return ASU_ERR_CUDA_BASE + static_cast<int>(e);
-        }
-        configured |= 1ull << dev;
-    }
-    if (smem > static_cast<size_t>(max_dynamic[dev])) return ASU_ERR_ARG;
+    int max_dynamic = 0;
+    const int rc = asu_max_dynamic_smem(reinterpret_cast<const void*>(lru_step_kernel<IPT_Q, IPT_S>), &max_dynamic);
+    if (rc != ASU_OK) return rc;
+    if (smem > static_cast<size_t>(max_dynamic)) return ASU_ERR_ARG;
     const uint32_t grid = R < 65535u ? R : 65535u;
     return launch_pdl(lru_step_kernel<IPT_Q, IPT_S>, dim3(grid), dim3(kThreads), smem, s, t2s, s2t, order, stack,
                       count, query, slot_out, hit, inst, evicted, ev_stride, ev_count, stats, status, R, K, S, Q,

@@ -437,7 +437,8 @@ extern "C" int asu_kv_resolver_do(void* stream, const int32_t* topk, int64_t top
         const int64_t entries = topk_numel - first < kMaxCopyEntries ? topk_numel - first : kMaxCopyEntries;
         const uint32_t c0 = static_cast<uint32_t>(kv0_row_bytes / vec), c1 = static_cast<uint32_t>(kv1_row_bytes / vec);
         int64_t grid = (entries * (c0 + c1) + kCopyThreads * kCopyUnroll - 1) / (kCopyThreads * kCopyUnroll);
-        if (grid > 148 * 4) grid = 148 * 4;
+        const int64_t cap = static_cast<int64_t>(asu_sm_count()) * 4;
+        if (grid > cap) grid = cap;
         if (grid < 1) grid = 1;
         rc = vec == 16 ? launch_copy<int4>(s, grid, ws, first, entries, kv0_src, kv1_src, kv0_dst, kv1_dst, c0, c1)
            : vec == 4  ? launch_copy<int32_t>(s, grid, ws, first, entries, kv0_src, kv1_src, kv0_dst, kv1_dst, c0, c1)

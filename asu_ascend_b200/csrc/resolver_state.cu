@@ -63,7 +63,8 @@ extern "C" int asu_resolver_reset(void* stream, int32_t* token_state, int32_t* a
         return ASU_ERR_ARG;
     int64_t work = max_seq_len > slot_count ? max_seq_len : slot_count;
     int64_t grid = (work + kThreads - 1) / kThreads;
-    if (grid > 148 * 16) grid = 148 * 16;
+    const int64_t cap = static_cast<int64_t>(asu_sm_count()) * 16;
+    if (grid > cap) grid = cap;
     resolver_reset_kernel<<<static_cast<uint32_t>(grid), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
         token_state, asu_record_addr, hbm_slot_of_token, max_seq_len, slot_owner_token, free_slot_stack,
         free_slot_count, slot_count, block_table, block_size, actual_seq_len, managed_prefix_len);

@@ -109,7 +109,11 @@ swapin_kernel(const int4* host, int64_t pool_rows, uint32_t cpr, uint32_t pitch1
 // rows, 128-byte-aligned host rows read this way reach ~48 GB/s against ~44 GB/s for the
 // 16-byte-load kernel above; the copy engine (cudaMemcpyAsync of 256 MiB) reaches ~56 GB/s.
 // A wait that runs out sets ASU_ST_TIMEOUT, waits once more (bounded) for the copy still in
-// flight into the slot, and the lane stops.
+// flight into the slot, and the lane stops.  A bulk copy cannot be cancelled: if that second
+// wait runs out too, the copy may still land in this CTA's shared memory after the CTA has
+// exited, i.e. in whichever CTA the SM runs next.  ASU_ST_TIMEOUT therefore reports a failed
+// host link, not a skipped row: the results of this stream's later launches are not to be
+// trusted (the caller treats it like a CUDA error of the context).
 constexpr int kBulkWarps = 4;
 constexpr uint32_t kBulkMaxRow = 1024;
 constexpr int kBulkSpinLimit = 1 << 18;  // ~1 s of try_wait on B200 (each try suspends ~4 us)
@@ -215,31 +219,10 @@ namespace {
 
 // Dynamic shared memory limit of swapin_bulk_kernel, configured once per device.
 int bulk_configure(uint32_t smem) {
-    static uint64_t configured = 0;
-    static int max_dynamic[64];
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess || dev < 0 || dev >= 64) {
-        cudaGetLastError();
-        return e != cudaSuccess ? ASU_ERR_CUDA_BASE + static_cast<int>(e) : ASU_ERR_ARG;
-    }
-    if (!((configured >> dev) & 1ull)) {
-        int optin = 0;
-        cudaFuncAttributes fa;
-        e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, swapin_bulk_kernel);
-        if (e == cudaSuccess) {
-            max_dynamic[dev] = optin - static_cast<int>(fa.sharedSizeBytes);
-            e = cudaFuncSetAttribute(swapin_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     max_dynamic[dev]);
-        }
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            return ASU_ERR_CUDA_BASE + static_cast<int>(e);
-        }
-        configured |= 1ull << dev;
-    }
-    return smem <= static_cast<uint32_t>(max_dynamic[dev]) ? ASU_OK : ASU_ERR_ARG;
+    int max_dynamic = 0;
+    const int rc = asu_max_dynamic_smem(reinterpret_cast<const void*>(swapin_bulk_kernel), &max_dynamic);
+    if (rc != ASU_OK) return rc;
+    return smem <= static_cast<uint32_t>(max_dynamic) ? ASU_OK : ASU_ERR_ARG;
 }
 
 }  // namespace
@@ -266,14 +249,16 @@ extern "C" int asu_swapin_gather(void* stream, const void* host_pool, int64_t po
         if (rc != ASU_OK) return rc;
         uint64_t grid = (groups + kBulkWarps - 1) / kBulkWarps;
         const uint64_t per_sm = stride <= 768 ? 2 : 1;  // two CTAs per SM while their slots fit
-        if (grid > 148ull * per_sm) grid = 148ull * per_sm;
+        const uint64_t cap = static_cast<uint64_t>(asu_sm_count()) * per_sm;
+        if (grid > cap) grid = cap;
         return launch_pdl(swapin_bulk_kernel, dim3(static_cast<uint32_t>(grid)), dim3(kBulkWarps * 32), smem,
                           static_cast<cudaStream_t>(stream), static_cast<const uint8_t*>(host_pool), pool_rows,
                           row_bytes, host_pitch, record_addr, key_space, query, slot, install_mask, query_count,
                           static_cast<uint8_t*>(slot_pool), slot_count, req_num, status, stride);
     }
     uint64_t grid = (groups + kWarps - 1) / kWarps;
-    if (grid > 148ull * 8ull) grid = 148ull * 8ull;
+    const uint64_t cap = static_cast<uint64_t>(asu_sm_count()) * 8ull;
+    if (grid > cap) grid = cap;
     return launch_pdl(swapin_kernel, dim3(static_cast<uint32_t>(grid)), dim3(kWarps * 32), 0,
                       static_cast<cudaStream_t>(stream), static_cast<const int4*>(host_pool), pool_rows,
                       row_bytes / 16, host_pitch / 16, record_addr, key_space, query, slot, install_mask, query_count,

@@ -87,7 +87,8 @@ extern "C" int asu_host_pool_writeback(void* stream, void* host_pool, int64_t po
     const uint64_t total = static_cast<uint64_t>(n) * wpr;
     if (total >= (1ull << 31)) return ASU_ERR_ARG;  // split larger write-backs
     uint64_t grid = (total + kThreads * kUnroll - 1) / (kThreads * kUnroll);
-    if (grid > 148ull * 8ull) grid = 148ull * 8ull;
+    const uint64_t cap = static_cast<uint64_t>(asu_sm_count()) * 8ull;
+    if (grid > cap) grid = cap;
     writeback_kernel<<<static_cast<uint32_t>(grid), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<int4*>(host_pool), pool_rows, cpr, wpr, host_pitch / 16, static_cast<const int4*>(src), src_rows,
         src_pitch / 16, src_index, dst_row, static_cast<uint32_t>(n), status);

@@ -69,6 +69,9 @@ GATHER_DRAM_BYTES_PER_LAUNCH = 13.82e6                     # lookup workload, ga
 RESOLVE_DRAM_BYTES_PER_CALL = 0.903e6                      # decode workload, resolve_kernel (rows copied in-cluster)
 WRITEBACK_PCIE_WRITE_BYTES_PER_LAUNCH = 59.06e9 * 1.918e-3  # pcie__write_bytes.sum.per_second x duration
 OPS_LOOKUP_DRAM_BYTES_PER_LAUNCH = 0.213e6                  # ops workload, req 8 mixed
+# where the traffic figures come from (the kernel source they were captured on)
+SWAPIN_TRAFFIC_SOURCE = "profiles/swapin_bulk_kernel_c2.md (ncu capture of the swap-in kernel as of commit bd3ed66)"
+LRU_TRAFFIC_SOURCE = "profiles/lru_step_kernel_c2.md (ncu capture of the LRU kernel as of commit 9193eab)"
 
 
 @dataclass
@@ -277,6 +280,24 @@ def fold_layers(trace: np.ndarray, keys: int) -> np.ndarray:
     return (trace.astype(np.int64) + off).astype(np.int32)
 
 
+def trace_seed(args, first_request: int) -> int:
+    """Seed of the trace of the requests starting at global request index `first_request`; the
+    GPU arm's rank 0 and the reference arm use the same one."""
+    return args.seed + 1000 * (first_request + 1)
+
+
+def resolver_config(args, cfg: ResolverCfg, req_per_gpu: int, world: int) -> dict:
+    """The `config` object of a resolver-workload line; both arms print exactly this."""
+    job_req = cfg.req if cfg.strong else cfg.req * world
+    pitch = args.host_pitch or ((cfg.row + 127) // 128 * 128 if cfg.row <= 1024 else cfg.row)
+    return {"workload": cfg.describe(), "requests_per_gpu": req_per_gpu, "global_batch": job_req, "topk": cfg.topk,
+            "layers": cfg.layers, "context": cfg.keys, "slots_per_request": cfg.slots, "free_target": cfg.target,
+            "row_bytes": cfg.row,
+            "locality": (f"{int(cfg.reuse * 100)}% reuse + " + (f"zipf({cfg.zipf})" if cfg.zipf else "uniform")),
+            "host_pitch": pitch, "l2": L2_NOTE, "parallelism": f"request-sharded x{world}",
+            "prefill_steps": args.prefill, "trace_seed": trace_seed(args, 0)}
+
+
 # ------------------------------------------------------------------ CPU side
 
 CPU_CYCLE_STEPS = 32  # distinct top-k sets the CPU legs cycle through (fewer would repeat into hits)
@@ -328,11 +349,11 @@ def run_reference(args, world: int, rank: int):
     cfg = RESOLVER_WORKLOADS["resolver"]
     base = args.prefill + args.warmup
     cycle = max(args.steps, CPU_CYCLE_STEPS)
-    trace = make_trace(cfg, cfg.req, args.seed, base + cycle)
+    # rank 0's requests of the GPU arm: the same trace seed, the same top-k sets
+    trace = make_trace(cfg, cfg.req, trace_seed(args, 0), base + cycle)
     value, done, secs, miss = cpu_port_run(cfg, cfg.req, trace, base, cycle, args.cpu_sample_s, threads)
     line = base_line(world, args.steps, args.warmup, secs / done * 1e3, value,
-                     {"workload": cfg.describe(), "requests_per_gpu": cfg.req, "topk": cfg.topk,
-                      "context": cfg.keys, "slots_per_request": cfg.slots, "row_bytes": cfg.row})
+                     resolver_config(args, cfg, cfg.req, world))
     line.update({"impl": "reference", "cpu_steps_timed": done,
                  "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                                   "sample": f"{done} steps x {cfg.req} requests x top-k {cfg.topk} ({secs:.1f} s, "
@@ -427,7 +448,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     base = args.prefill + W
     cpu_leg = world == 1 and not args.no_cpu_baseline and cfg.name == "resolver"
     n_steps = base + (max(2 * K_steps, CPU_CYCLE_STEPS) if cpu_leg else 2 * K_steps)
-    trace = make_trace(cfg, R, args.seed + 1000 * (r0 + 1), n_steps)
+    trace = make_trace(cfg, R, trace_seed(args, r0), n_steps)
     q_dev = torch.from_numpy(trace).to(dev)
     q_host = torch.from_numpy(trace).pin_memory()
 
@@ -461,6 +482,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(L)] for _ in range(K_steps)]
     free_before = torch.empty(K_steps * L, dtype=torch.int64, device=dev)
     free_after = torch.empty(K_steps * L, dtype=torch.int64, device=dev)
+    evicting = torch.empty(K_steps * L, dtype=torch.int64, device=dev)  # request-steps that evicted
     stats0 = total_stats().clone()
     clocks = ClockSampler(gpu_index(local_rank))
     clocks.start()
@@ -479,13 +501,15 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             host.swapin(recs[layer], q, o.slot, o.install, slot_pools[layer], status=status)
             c.record()
             free_after[k * L + layer] = pools[layer].free_count.sum()
+            evicting[k * L + layer] = (o.evicted_count > 0).sum()
     rank_sync(torch)
     clk = clocks.stop()
     resolve_ms = [a.elapsed_time(b) for step in ev for a, b, _ in step]
     swapin_ms = [b.elapsed_time(c) for step in ev for _, b, c in step]
     step_ms = [sum(a.elapsed_time(c) for a, _, c in step) for step in ev]
     d_stats = (total_stats() - stats0).cpu().tolist()
-    installs, evictions = int(d_stats[2]), int(d_stats[4])
+    misses, installs, evictions = int(d_stats[1]), int(d_stats[2]), int(d_stats[4])
+    n_evicting = int(evicting.sum().item())
     res0 = R * cfg.slots * K_steps * L - int(free_before.sum().item())
     res2 = R * cfg.slots * K_steps * L - int(free_after.sum().item())
 
@@ -530,7 +554,12 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
         peaks = load_peaks()
         hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
         launches = K_steps * L
-        alg_bytes = launches * R * cfg.topk * 14 + 4 * (res0 + res2) + 12 * installs + 20 * evictions
+        # lookup + LRU maintain bytes by the survey's formula: 13 B/query (lookup) + 4 B/query
+        # (touch) + 24 B/miss + 12 B/eviction + 4 B x slots per request-step that evicts
+        alg_bytes = (launches * R * cfg.topk * (13 + 4) + 24 * misses + 12 * evictions
+                     + 4 * cfg.slots * n_evicting)
+        # the kernel's own accounting (order rows read and written, 14 B/query, map updates)
+        kernel_bytes = launches * R * cfg.topk * 14 + 4 * (res0 + res2) + 12 * installs + 20 * evictions
         achieved = alg_bytes / (sum(resolve_ms) * 1e-3) / 1e9
         swap_gbs = installs * cfg.row / (sum(swapin_ms) * 1e-3) / 1e9
         cpu = None
@@ -543,14 +572,8 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
                    "sample": f"{done} steps x {R} requests x top-k {cfg.topk} ({secs:.1f} s, cycling {cycle} "
                              f"top-k sets of this workload; CPU miss rate {miss:.3f}), C restatement of "
                              "LRUManagedCache + row memcpy, all host threads"}
-        config = {"workload": cfg.describe(), "requests_per_gpu": R, "global_batch": job_req, "topk": cfg.topk,
-                  "layers": L, "context": cfg.keys, "slots_per_request": cfg.slots, "free_target": cfg.target,
-                  "row_bytes": cfg.row,
-                  "locality": (f"{int(cfg.reuse * 100)}% reuse + "
-                               + (f"zipf({cfg.zipf})" if cfg.zipf else "uniform")),
-                  "host_pitch": host.pitch, "host_cpus_bound": len(bound_cpus), "l2": L2_NOTE,
-                  "parallelism": f"request-sharded x{world}",
-                  "prefill_steps": args.prefill}
+        config = resolver_config(args, cfg, R, world)
+        assert config["host_pitch"] == host.pitch
         line = base_line(world, K_steps, W, max_ms / K_steps, idx_per_step * K_steps / (max_ms * 1e-3), config,
                          scaling="strong" if cfg.strong else "weak")
         line.update({
@@ -567,6 +590,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
                                      if cfg.row == 656 and host.pitch == 768 else None),
                          "traffic_kind": "PCIe read bytes per launch (ncu pcie__read_bytes of the resolver "
                                          "workload, scaled to this run's installs per launch)",
+                         "traffic_source": SWAPIN_TRAFFIC_SOURCE,
                          "peak_source": ("pinned cudaMemcpyAsync H2D 256 MiB, best of 10, this run"
                                          + ("" if world == 1 else ", all ranks copying at once")),
                          "peak_alone": h2d_alone},
@@ -574,12 +598,19 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
                              "unit": "GB/s", "frac": achieved / hbm_peak,
                              "traffic": LRU_DRAM_BYTES_PER_LAUNCH if cfg.name == "resolver" else None,
                              "traffic_kind": "dram__bytes_read.sum + dram__bytes_write.sum of one launch (ncu)",
+                             "traffic_source": LRU_TRAFFIC_SOURCE,
                              "algorithmic_bytes_per_launch": alg_bytes / launches,
+                             "byte_formula": "17 B/query (13 lookup + 4 touch) + 24 B/unique miss + 12 B/eviction "
+                                             "+ 4 B x slots per request-step with evictions",
+                             "kernel_bytes_per_launch": kernel_bytes / launches,
+                             "frac_of_traffic": ((LRU_DRAM_BYTES_PER_LAUNCH / (statistics.fmean(resolve_ms) * 1e-3)
+                                                  / 1e9 / hbm_peak) if cfg.name == "resolver" else None),
                              "peak_source": "measured HBM copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"},
             "e2e": {"value": idx_per_step * K_steps / (max_e2e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": R * cfg.topk * 4 * L, "d2h_bytes_per_step": R * cfg.topk * 5 * L},
             "gpu_launches": 2 * launches,
             "job_stats": dict(zip(LruSlotPools.STAT_NAMES, job_stats)),
+            "host_cpus_bound": len(bound_cpus),
             "note_step_time": "sum over layers of (resolve + swap-in) event intervals",
             "cpu_baseline": cpu,
             "clocks": clk,

@@ -44,7 +44,9 @@ extern "C" {
 #define ASU_ST_BAD_SOURCE 0x20      /* swap-in / resolver: source row out of range */
 #define ASU_ST_BAD_TOKEN_STATE 0x40 /* resolver: token_state not in {ASU_ONLY, HBM_RESIDENT, TAIL_HBM} */
 #define ASU_ST_NO_VICTIM 0x80       /* batch-LRU: more unique misses than evictable slots (state left unchanged) */
-#define ASU_ST_TIMEOUT 0x100        /* swap-in: a bulk copy did not complete within its wait limit (rows skipped) */
+#define ASU_ST_TIMEOUT 0x100        /* swap-in: a bulk copy did not complete within its wait limit (rows skipped);
+                                       a late copy may still land in shared memory, so the stream's later
+                                       results are not to be trusted: handle it like a context error */
 
 /* ---- reference constants (ops/asu_hbm_index_lookup_aiv.cpp:7-12) ------- */
 #define ASU_HBM_INDEX_SIZE (128u * 1024u)

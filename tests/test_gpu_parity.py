@@ -546,31 +546,65 @@ def test_lru_stress_shape_against_oracle():
     _lru_run_and_compare(pools, oracle, steps, check_state_every=5)
 
 
-def test_lru_full_stress_size_invariants():
-    """The full stress size (128 requests, 1M-token key space): after every step the two maps are
-    inverse to each other, the order row lists exactly the resident slots, the free stack the
-    others, and each request's installs went to distinct slots -- properties that do not need
-    an oracle run at this size."""
+def _c_oracle_compare_step(out, res, tag):
+    """One step of every request: GPU outputs against the C oracle's (slot, hit, install,
+    evicted ids and counts)."""
+    slot, hit, inst, ev, evn = res
+    np.testing.assert_array_equal(N(out.slot), slot, err_msg=f"{tag} slot")
+    np.testing.assert_array_equal(N(out.hit), hit, err_msg=f"{tag} hit")
+    np.testing.assert_array_equal(N(out.install), inst, err_msg=f"{tag} install")
+    gev, gevn = N(out.evicted), N(out.evicted_count)
+    np.testing.assert_array_equal(gevn, evn, err_msg=f"{tag} evicted count")
+    for r in range(gevn.shape[0]):
+        np.testing.assert_array_equal(gev[r, : gevn[r]], ev[r, : evn[r]], err_msg=f"{tag} req {r} evicted")
+
+
+def _c_oracle_compare_state(pools, cpools, tag):
+    """Final state of every request against the C oracle: slot_to_token, the resident part of
+    the order row, the free part of the stack and the free count.  token_to_slot is checked as
+    the inverse of slot_to_token (every resident key maps back to its slot and no other key
+    maps anywhere), which with slot_to_token equal to the oracle's makes it equal too, without
+    copying the whole [R, key_space] table back."""
+    S = pools.slot_count
+    s2t, order, stack, count = (N(x) for x in (pools.slot_to_token, pools.lru_order, pools.free_stack,
+                                               pools.free_count))
+    for r in range(pools.req_num):
+        _, es2t, eorder, estack, ecount = cpools.export(r)
+        assert count[r] == ecount, f"{tag} req {r} free count"
+        np.testing.assert_array_equal(s2t[r], es2t, err_msg=f"{tag} req {r} slot_to_token")
+        np.testing.assert_array_equal(order[r, : S - ecount], eorder[: S - ecount], err_msg=f"{tag} req {r} order")
+        np.testing.assert_array_equal(stack[r, :ecount], estack[:ecount], err_msg=f"{tag} req {r} free stack")
+    gs2t = pools.slot_to_token
+    rows, slots = torch.nonzero(gs2t >= 0, as_tuple=True)
+    assert torch.equal(pools.token_to_slot[rows, gs2t[rows, slots].long()], slots.int()), tag
+    assert int((pools.token_to_slot >= 0).sum()) == rows.numel(), tag
+
+
+def test_lru_full_stress_size_against_c_oracle():
+    """The full stress size (128 requests, 1M-token key space, 8192 slots, target 2048, uniform
+    top-k 2048 with 20% reuse, ~80% misses): every request against the multi-threaded C oracle
+    for six steps -- per-step outputs and evicted ids, final state -- plus, after every step,
+    the map invariants that need no oracle (maps inverse to each other, the order row holding
+    exactly the resident slots and the free stack the others, installs to distinct slots)."""
     from asu_ascend_b200.lru import LruSlotPools
     from asu_ascend_b200.workloads import FastLocalityTrace
+    from oracle import c_oracle as CO
 
     R, K, S = 128, 1 << 20, 8192
     tr = FastLocalityTrace(R, K, topk=2048, reuse=0.2, zipf_s=None, seed=78)
     pools = LruSlotPools(R, K, S, 2048, 2048, device=DEV)
+    cpools = CO.LruPools(R, K, S, 2048)
     ar = torch.arange(S, device=DEV)
-    for _ in range(4):
-        q = T(tr.step())
-        out = pools.step(q)
+    for step in range(6):
+        q = tr.step()
+        out = pools.step(T(q))
+        _c_oracle_compare_step(out, cpools.step_all(q), f"step {step}")
         free = pools.free_count.long()
         s2t = pools.slot_to_token
         resident = s2t >= 0
         assert torch.equal(resident.sum(1), S - free)
-        rows, slots = torch.nonzero(resident, as_tuple=True)
-        assert torch.equal(pools.token_to_slot[rows, s2t[rows, slots].long()], slots.int())
-        assert int((pools.token_to_slot >= 0).sum()) == int(resident.sum())
         order_ok = ar[None, :] < (S - free)[:, None]
         ordered = torch.where(order_ok, pools.lru_order, torch.full_like(pools.lru_order, -1))
-        assert torch.equal(torch.sort(ordered, 1).values[:, -1].ge(0), (S - free) > 0)
         marks = torch.zeros((R, S), dtype=torch.int32, device=DEV)
         marks.scatter_add_(1, ordered.clamp(min=0).long(), order_ok.int())
         assert torch.equal(marks > 0, resident) and int(marks.max()) <= 1
@@ -583,41 +617,33 @@ def test_lru_full_stress_size_invariants():
         imarks = torch.zeros((R, S), dtype=torch.int32, device=DEV)
         imarks.scatter_add_(1, islots.clamp(min=0).long(), inst.int())
         assert int(imarks.max()) <= 1
-        assert bool((out.slot[out.hit | out.install] >= 0).all())
+    _c_oracle_compare_state(pools, cpools, "stress final")
     pools.check_status()
+    cpools.close()
 
 
-def test_lru_multilayer_batch_of_1024_requests():
-    """The request-sharded configuration's per-GPU batch at one GPU: 1024 requests (several
-    waves of CTAs), 131072 tokens, 8192 slots, top-k 2048.  Requests 0, 511 and 1023 are checked
-    against the oracle step by step, and the state of all of them for the map invariants."""
+def test_lru_multilayer_1024_requests_4_layers_against_c_oracle():
+    """The request-sharded configuration's batch on one GPU: 1024 requests (several waves of
+    CTAs), 4 layers with independent top-k sets, each (layer, request) with its own 8192-slot
+    pool over 131072 tokens, top-k 2048, target 2048.  Every (layer, request) against the C
+    oracle for four steps: per-step outputs and evicted ids, then the final state."""
     from asu_ascend_b200.lru import LruSlotPools
     from asu_ascend_b200.workloads import FastLocalityTrace
+    from oracle import c_oracle as CO
 
-    R, K, S = 1024, 131072, 8192
-    tr = FastLocalityTrace(R, K, topk=2048, seed=79)
-    pools = LruSlotPools(R, K, S, 2048, 2048, device=DEV)
-    picks = (0, 511, 1023)
-    oracle = {r: O.LruPool(S, 2048) for r in picks}
-    for _ in range(4):
-        q = tr.step()
-        out = pools.step(T(q))
-        slot, hit, inst = N(out.slot), N(out.hit), N(out.install)
-        for r in picks:
-            res = oracle[r].step(q[r])
-            np.testing.assert_array_equal(slot[r], res.slot)
-            np.testing.assert_array_equal(hit[r], res.hit)
-            np.testing.assert_array_equal(inst[r], res.install)
-    for r in picks:
-        et2s, es2t, eorder, estack, ecount = oracle[r].export_state(K)
-        assert int(N(pools.free_count)[r]) == ecount
-        np.testing.assert_array_equal(N(pools.slot_to_token[r]), es2t)
-        np.testing.assert_array_equal(N(pools.lru_order[r])[: S - ecount], eorder[: S - ecount])
-    s2t = pools.slot_to_token
-    rows, slots = torch.nonzero(s2t >= 0, as_tuple=True)
-    assert torch.equal(pools.token_to_slot[rows, s2t[rows, slots].long()], slots.int())
-    assert int((pools.token_to_slot >= 0).sum()) == rows.numel()
-    pools.check_status()
+    R, K, S, L = 1024, 131072, 8192, 4
+    traces = [FastLocalityTrace(R, K, topk=2048, seed=79 + 7919 * layer) for layer in range(L)]
+    pools = [LruSlotPools(R, K, S, 2048, 2048, device=DEV) for _ in range(L)]
+    cpools = [CO.LruPools(R, K, S, 2048) for _ in range(L)]
+    for step in range(4):
+        for layer in range(L):
+            q = traces[layer].step()
+            out = pools[layer].step(T(q))
+            _c_oracle_compare_step(out, cpools[layer].step_all(q), f"step {step} layer {layer}")
+    for layer in range(L):
+        _c_oracle_compare_state(pools[layer], cpools[layer], f"layer {layer} final")
+        pools[layer].check_status()
+        cpools[layer].close()
 
 
 def test_lru_c2_shape_against_oracle():
