@@ -70,6 +70,11 @@ _SIGS = {
     "asu_resolver_reset": [_P, _P, _P, _P, c_int64, _P, _P, _P, c_int64, _P, c_int64, c_int64, c_int64, c_int64],
     "asu_kv_resolver_noalloc": [_P, _P, c_int64, _P, _P, _P, _P, _P, _P, c_int64, _P, c_int64, _P, _P, _P, _P,
                                 c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, _P, _P],
+    "asu_resolver_reset_layers": [_P, c_int64, _P, _P, _P, c_int64, _P, _P, _P, c_int64, _P, c_int64, c_int64,
+                                  c_int64, c_int64],
+    "asu_resolver_mark_token": [_P, c_int64, _P, c_int64, c_int64],
+    "asu_kv_resolver_lru": [_P, _P, c_int64, _P, _P, _P, _P, _P, _P, _P, c_int64, c_int64, _P, c_int64, _P, _P, _P,
+                            _P, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, _P, _P, _P, _P, _P],
 }
 _RESTYPE = {"asu_status_string": c_char_p, "asu_kv_resolver_workspace_bytes": c_int64}
 

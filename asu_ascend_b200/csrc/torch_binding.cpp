@@ -29,6 +29,7 @@
 #include <torch/library.h>
 
 #include <atomic>
+#include <optional>
 #include <sstream>
 #include <tuple>
 #include <string>
@@ -189,6 +190,97 @@ at::Tensor resolve_meta(const at::Tensor& original_topk_indices, int64_t, int64_
                         const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
                         const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
                         int64_t) {
+    return at::empty(original_topk_indices.sizes(), original_topk_indices.options().dtype(at::kInt));
+}
+
+// ---------------------------------------------------------------------------------------------
+// resolver over a bounded managed pool (exact-LRU eviction); no reference counterpart: it is the
+// resolver of patch/0001 composed with simu/kv_cache_eviction_sim.py's LRUManagedCache, so the
+// managed cache can be smaller than the context.  Same argument checks as the resolver op, plus
+// the recency order row and the free target.
+
+at::Tensor resolve_lru_cuda(const at::Tensor& original_topk_indices, int64_t actual_seq_len,
+                            int64_t managed_prefix_len, const at::Tensor& token_state,
+                            const at::Tensor& asu_record_addr, const at::Tensor& hbm_slot_of_token,
+                            const at::Tensor& slot_owner_token, const at::Tensor& free_slot_stack,
+                            const at::Tensor& free_slot_count, const at::Tensor& lru_order, int64_t free_target,
+                            const at::Tensor& original_block_table, const at::Tensor& original_kv_cache_0,
+                            const at::Tensor& original_kv_cache_1, const at::Tensor& managed_kv_cache_0,
+                            const at::Tensor& managed_kv_cache_1, int64_t block_size,
+                            const std::optional<at::Tensor>& stats) {
+    (void)managed_prefix_len;
+    Prepared p = prepare(original_topk_indices, actual_seq_len, token_state, asu_record_addr, hbm_slot_of_token,
+                         slot_owner_token, free_slot_stack, free_slot_count, original_block_table,
+                         original_kv_cache_0, original_kv_cache_1, managed_kv_cache_0, managed_kv_cache_1,
+                         block_size);
+    const c10::Device dev = token_state.device();
+    req_cuda_i32("free_slot_stack", free_slot_stack, dev);  // written: evictions push on it
+    req_cuda_i32("lru_order", lru_order, dev);
+    TORCH_CHECK_VALUE(free_target >= 0, "free_target must be non-negative");
+    int64_t* stats_ptr = nullptr;
+    if (stats.has_value() && stats->defined()) {
+        TORCH_CHECK(stats->scalar_type() == at::kLong && stats->device() == dev && stats->is_contiguous() &&
+                        stats->numel() == ASU_LRU_STAT_COLS,
+                    "stats must be a contiguous int64 tensor of ", ASU_LRU_STAT_COLS, " elements on ", dev);
+        stats_ptr = stats->data_ptr<int64_t>();
+    }
+    const c10::cuda::CUDAGuard guard(dev);
+    at::Tensor resolved = at::empty(original_topk_indices.sizes(), token_state.options().dtype(at::kInt));
+    const int64_t n = p.topk.numel();
+    TORCH_CHECK_VALUE(n <= 4096, "npu_asu_resolve_kv_slots_lru takes at most 4096 top-k entries, got ", n);
+    const at::Tensor &o0 = original_kv_cache_0, &o1 = original_kv_cache_1;
+    const at::Tensor &m0 = managed_kv_cache_0, &m1 = managed_kv_cache_1;
+    const int64_t slot_count = std::min({m0.size(0), m1.size(0), slot_owner_token.numel(), free_slot_stack.numel(),
+                                         lru_order.numel()});
+    TORCH_CHECK_VALUE(slot_count > 0 && slot_count <= 16384, "managed slot count must be in [1, 16384], got ",
+                      slot_count);
+    const int64_t src_rows = std::min(o0.size(0), o1.size(0));
+    const int64_t max_seq = std::min({token_state.numel(), hbm_slot_of_token.numel(), p.record.numel()});
+    const bool checks = g_status_checks.load(std::memory_order_relaxed);
+    at::Tensor status = checks ? at::zeros({1}, token_state.options()) : at::Tensor();
+    const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev.index()).stream();
+    const int rc = asu_kv_resolver_lru(
+        stream, p.topk.data_ptr<int32_t>(), n, token_state.data_ptr<int32_t>(), p.record.data_ptr<int32_t>(),
+        hbm_slot_of_token.data_ptr<int32_t>(), slot_owner_token.data_ptr<int32_t>(),
+        free_slot_stack.data_ptr<int32_t>(), free_slot_count.data_ptr<int32_t>(), lru_order.data_ptr<int32_t>(),
+        slot_count, free_target, p.block_table.data_ptr<int32_t>(), p.block_table.numel(), o0.data_ptr(),
+        o1.data_ptr(), m0.data_ptr(), m1.data_ptr(), row_bytes(o0), row_bytes(o1), src_rows, max_seq,
+        actual_seq_len, block_size, resolved.data_ptr<int32_t>(), nullptr, nullptr, stats_ptr,
+        checks ? status.data_ptr<int32_t>() : nullptr);
+    TORCH_CHECK(rc == ASU_OK, "npu_asu_resolve_kv_slots_lru failed: ", asu_status_string(rc), " (code ", rc, ")");
+    if (checks) {
+        const int bits = status.item<int32_t>();
+        if (bits != 0) {
+            std::ostringstream hex;
+            hex << std::hex << bits;
+            TORCH_CHECK(false, "npu_asu_resolve_kv_slots_lru: device status ", status_list(bits), " (0x", hex.str(),
+                        ")");
+        }
+    }
+    return resolved;
+}
+
+at::Tensor resolve_lru_cpu(const at::Tensor& original_topk_indices, int64_t actual_seq_len,
+                           int64_t managed_prefix_len, const at::Tensor& token_state,
+                           const at::Tensor& asu_record_addr, const at::Tensor& hbm_slot_of_token,
+                           const at::Tensor& slot_owner_token, const at::Tensor& free_slot_stack,
+                           const at::Tensor& free_slot_count, const at::Tensor&, int64_t,
+                           const at::Tensor& original_block_table, const at::Tensor& original_kv_cache_0,
+                           const at::Tensor& original_kv_cache_1, const at::Tensor& managed_kv_cache_0,
+                           const at::Tensor& managed_kv_cache_1, int64_t block_size,
+                           const std::optional<at::Tensor>&) {
+    (void)managed_prefix_len;
+    prepare(original_topk_indices, actual_seq_len, token_state, asu_record_addr, hbm_slot_of_token, slot_owner_token,
+            free_slot_stack, free_slot_count, original_block_table, original_kv_cache_0, original_kv_cache_1,
+            managed_kv_cache_0, managed_kv_cache_1, block_size);
+    TORCH_CHECK(false, "npu_asu_resolve_kv_slots_lru needs CUDA tensors (asu_ascend_b200 has no CPU implementation)");
+}
+
+at::Tensor resolve_lru_meta(const at::Tensor& original_topk_indices, int64_t, int64_t, const at::Tensor&,
+                            const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                            const at::Tensor&, const at::Tensor&, int64_t, const at::Tensor&, const at::Tensor&,
+                            const at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t,
+                            const std::optional<at::Tensor>&) {
     return at::empty(original_topk_indices.sizes(), original_topk_indices.options().dtype(at::kInt));
 }
 
@@ -364,6 +456,13 @@ constexpr const char* kSchema =
     "Tensor free_slot_stack, Tensor! free_slot_count, Tensor original_block_table, Tensor original_kv_cache_0, "
     "Tensor original_kv_cache_1, Tensor! managed_kv_cache_0, Tensor! managed_kv_cache_1, int block_size) -> Tensor";
 
+constexpr const char* kLruSchema =
+    "npu_asu_resolve_kv_slots_lru(Tensor original_topk_indices, int actual_seq_len, int managed_prefix_len, "
+    "Tensor! token_state, Tensor asu_record_addr, Tensor! hbm_slot_of_token, Tensor! slot_owner_token, "
+    "Tensor! free_slot_stack, Tensor! free_slot_count, Tensor! lru_order, int free_target, "
+    "Tensor original_block_table, Tensor original_kv_cache_0, Tensor original_kv_cache_1, "
+    "Tensor! managed_kv_cache_0, Tensor! managed_kv_cache_1, int block_size, Tensor(s!)? stats=None) -> Tensor";
+
 }  // namespace
 
 #define ASU_DEFINE_OPS(m)    \
@@ -386,6 +485,12 @@ TORCH_LIBRARY_IMPL(asu, CPU, m) { ASU_IMPL_OPS(m, resolve_cpu, lookup_cpu, maint
 TORCH_LIBRARY_IMPL(_C_ascend, CPU, m) { ASU_IMPL_OPS(m, resolve_cpu, lookup_cpu, maintain_cpu, simt_cpu) }
 TORCH_LIBRARY_IMPL(asu, Meta, m) { ASU_IMPL_OPS(m, resolve_meta, lookup_meta, maintain_meta, simt_meta) }
 TORCH_LIBRARY_IMPL(_C_ascend, Meta, m) { ASU_IMPL_OPS(m, resolve_meta, lookup_meta, maintain_meta, simt_meta) }
+
+// The bounded-pool resolver is this library's own operator: registered under `asu` only.
+TORCH_LIBRARY_FRAGMENT(asu, m) { m.def(kLruSchema); }
+TORCH_LIBRARY_IMPL(asu, CUDA, m) { m.impl("npu_asu_resolve_kv_slots_lru", &resolve_lru_cuda); }
+TORCH_LIBRARY_IMPL(asu, CPU, m) { m.impl("npu_asu_resolve_kv_slots_lru", &resolve_lru_cpu); }
+TORCH_LIBRARY_IMPL(asu, Meta, m) { m.impl("npu_asu_resolve_kv_slots_lru", &resolve_lru_meta); }
 
 // Status checks of the op (synchronise after each call and raise on a device status); the Python
 // side's ops.set_status_checks() forwards here.

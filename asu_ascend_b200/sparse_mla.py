@@ -25,13 +25,14 @@ from .ops import status_checks_enabled
 
 
 def contexts_for_mla(kv_caches: dict[str, torch.Tensor], max_seq_len: int, block_size: int,
-                     managed_slot_count: int | None = None,
-                     enabled: bool | None = None) -> _manager.ASUFullKVCacheManagerFunctional:
-    """Manager over vLLM MLA caches ``[num_blocks, block_size, row]`` (one per layer)."""
+                     managed_slot_count: int | None = None, enabled: bool | None = None,
+                     free_target: int | None = None) -> _manager.ASUFullKVCacheManagerFunctional:
+    """Manager over vLLM MLA caches ``[num_blocks, block_size, row]`` (one per layer); a
+    ``free_target`` makes every layer's pool an exact-LRU cache."""
     pairs = {name: (c, c.new_empty((*c.shape[:2], 0))) for name, c in kv_caches.items()
              if isinstance(c, torch.Tensor) and c.dim() == 3}
     mgr = _manager.ASUFullKVCacheManagerFunctional.from_kv_caches(pairs, max_seq_len, block_size,
-                                                                  managed_slot_count, enabled)
+                                                                  managed_slot_count, enabled, free_target)
     for name in pairs:
         if mgr.has_layer(name):  # whole pages, so FlashMLA's paged fp8 decode can read it (rows past the slots unused)
             ctx = mgr.get_layer_context(name)
@@ -60,7 +61,8 @@ def resolve_topk(ctx: _manager.ASULayerKVCacheContext, topk_indices: torch.Tenso
     """Managed slots of one request's top-k ``[num_tokens, topk]`` (-1 entries stay -1).
 
     Missing tokens are installed into the managed cache (rows copied from the paged
-    ``kv_cache``) exactly as ``npu_asu_resolve_kv_slots_single_req`` does; the call is
+    ``kv_cache``) exactly as ``npu_asu_resolve_kv_slots_single_req`` does -- through its
+    exact-LRU variant (``asu_kv_resolver_lru``) when the layer's pool evicts; the call is
     asynchronous on the current stream.
     """
     dev = ctx.token_state.device
@@ -81,8 +83,21 @@ def resolve_topk(ctx: _manager.ASULayerKVCacheContext, topk_indices: torch.Tenso
         return out
     row_bytes = kv_cache.shape[2] * kv_cache.element_size()
     src_rows = kv_cache.shape[0] * kv_cache.shape[1]
-    ws = torch.empty(int(lib.asu_kv_resolver_workspace_bytes(n)), dtype=torch.uint8, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev) if status_checks_enabled() else None
+    if ctx.bounded:
+        with torch.cuda.device(dev):
+            check(lib.asu_kv_resolver_lru(
+                torch.cuda.current_stream(dev).cuda_stream, topk_indices.data_ptr(), n, ctx.token_state.data_ptr(),
+                ctx.asu_record_addr.data_ptr(), ctx.hbm_slot_of_token.data_ptr(), ctx.slot_owner_token.data_ptr(),
+                ctx.free_slot_stack.data_ptr(), ctx.free_slot_count.data_ptr(), ctx.lru_order.data_ptr(),
+                ctx.managed_slot_count, ctx.free_target, bt.data_ptr(), bt.numel(), kv_cache.data_ptr(), None,
+                m.data_ptr(), None, row_bytes, 0, src_rows, ctx.max_seq_len, ctx.actual_seq_len, ctx.block_size,
+                out.data_ptr(), None, None, ctx.lru_stats.data_ptr(), None if status is None else status.data_ptr()),
+                "resolve_topk")
+        if status is not None:
+            raise_on_status(status, "resolve_topk", ST_BAD_QUERY)
+        return out
+    ws = torch.empty(int(lib.asu_kv_resolver_workspace_bytes(n)), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
         check(lib.asu_kv_resolver_do(
             torch.cuda.current_stream(dev).cuda_stream, topk_indices.data_ptr(), n, ctx.token_state.data_ptr(),

@@ -23,6 +23,8 @@ Other workloads (`--workload`):
   stress-block  the stress context in 64-token blocks: top-k 32 blocks, 128 block slots,
                 41,984-byte rows
   decode        1 request, 61 layers x npu_asu_resolve_kv_slots_single_req per decode step
+  decode-lru    the decode workload over exact-LRU managed pools of 8192 + 2048 slots per layer
+                (free target 2048) through npu_asu_resolve_kv_slots_lru
   writeback     prefill write-back of a 128K-token context x 4 layers into the pinned pool
   ops           asu_hbm_index_lookup / asu_hbm_index_maintain as the reference's op benchmark runs
                 them (req_num 1-8, hit/miss/mixed, state restored per call, 200 calls), plus the
@@ -115,7 +117,7 @@ def parse_args():
     p.add_argument("--prefill", type=int, default=8)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--workload", choices=("resolver", "lru1", "lookup", "multilayer", "stress", "stress-block", "decode",
-                            "writeback", "ops"),
+                                          "decode-lru", "writeback", "ops"),
                    default="resolver")
     p.add_argument("--seed", type=int, default=2026)
     p.add_argument("--cpu-sample-s", type=float, default=12.0)
@@ -775,13 +777,16 @@ DECODE_BLOCK = 128
 DECODE_TOPK = 2048
 DECODE_ROW0 = 512           # kv0 (latent) bf16 elements per token
 DECODE_ROW1 = 64            # kv1 (rope) bf16 elements per token
+DECODE_LRU_SLOTS = 8192 + 2048  # decode-lru: managed slots per layer (8192 resident + 2048 free)
+DECODE_LRU_TARGET = 2048        # decode-lru: free slots kept before each resolve
 
 
-def decode_cpu_leg(trace, bt, actual0, prefix, slots, src_rows, base, steps, cap_s):
-    """The Python restatement of the reference resolver with real bf16 row copies, on the same
-    per-layer top-k as the GPU run.  A round resets one layer's state, replays the prefill and
-    warm-up steps untimed and times the timed steps; rounds cycle over the layers until about
-    cap_s seconds of timed work.  Returns (timed calls, timed seconds)."""
+def decode_cpu_leg(trace, bt, actual0, prefix, slots, src_rows, base, steps, cap_s, free_target=None):
+    """The Python restatement of the reference resolver (composed with the LRU pool when
+    free_target is given) with real bf16 row copies, on the same per-layer top-k as the GPU run.
+    A round resets one layer's state, replays the prefill and warm-up steps untimed and times
+    the timed steps; rounds cycle over the layers until about cap_s seconds of timed work.
+    Returns (timed calls, timed seconds)."""
     from oracle import asu_oracle as O
 
     src_a = np.zeros((src_rows, DECODE_ROW0), np.uint16)
@@ -792,11 +797,16 @@ def decode_cpu_leg(trace, bt, actual0, prefix, slots, src_rows, base, steps, cap
     for rnd in range(trace.shape[1] * 64):
         layer = rnd % trace.shape[1]
         st = O.reset_state(DECODE_MAX_SEQ, slots, DECODE_BLOCK, actual0, prefix, bt)
+        order = np.full(slots, -1, np.int32)
         seq = actual0
         for i in range(base + steps):
             t0 = time.perf_counter()
-            O.resolve_kv_slots_single_req(trace[i, layer].reshape(1, 1, -1), seq, *st, bt, src_a, src_b, dst_a,
-                                          dst_b, DECODE_BLOCK)
+            if free_target is None:
+                O.resolve_kv_slots_single_req(trace[i, layer].reshape(1, 1, -1), seq, *st, bt, src_a, src_b, dst_a,
+                                              dst_b, DECODE_BLOCK)
+            else:
+                O.resolve_kv_slots_lru(trace[i, layer], seq, *st, order, free_target, bt, src_a, src_b, dst_a, dst_b,
+                                       DECODE_BLOCK)
             if i >= base:
                 timed += time.perf_counter() - t0
                 calls += 1
@@ -815,7 +825,8 @@ def run_decode(args, world: int, rank: int, local_rank: int):
     per-layer top-k of 2048 (70% reuse + Zipf 1.1 locality; the newest token always
     included), bf16 KV rows of 512 + 64 elements copied paged cache -> managed cache on a
     miss, managed slots = max_seq_len (the manager's default).  After every step the
-    request appends one decode token.
+    request appends one decode token.  `decode-lru`: every layer's managed pool is an exact-LRU
+    cache of 8192 + 2048 slots keeping 2048 free, resolved by `npu_asu_resolve_kv_slots_lru`.
     """
     import torch
 
@@ -845,7 +856,11 @@ def run_decode(args, world: int, rank: int, local_rank: int):
         kv1 = torch.randn((phys, bs, 1, DECODE_ROW1), device=dev, generator=g, dtype=torch.bfloat16)
         caches[f"layers.{layer}.self_attn"] = (kv0, kv1)
     bt = torch.randperm(phys, device=dev, generator=g)[:nblk].to(torch.int32).reshape(1, nblk)
-    mgr = M.ASUFullKVCacheManagerFunctional.from_kv_caches(caches, DECODE_MAX_SEQ, bs, enabled=True)
+    lru = args.workload == "decode-lru"
+    target = DECODE_LRU_TARGET if lru else None
+    mgr = M.ASUFullKVCacheManagerFunctional.from_kv_caches(caches, DECODE_MAX_SEQ, bs, enabled=True,
+                                                           managed_slot_count=DECODE_LRU_SLOTS if lru else None,
+                                                           free_target=target)
     mgr.reset_single_request(f"decode-req-{rank}", actual0, prefix, bt)
     ctxs = [mgr.get_layer_context(f"layers.{layer}.self_attn") for layer in range(L)]
     views = [c.original_kv_cache_views(caches[c.layer_name]) for c in ctxs]
@@ -860,10 +875,18 @@ def run_decode(args, world: int, rank: int, local_rank: int):
     out_host = torch.empty((L, 1, 1, DECODE_TOPK), dtype=torch.int32, pin_memory=True)
     out_dev = torch.empty((L, 1, 1, DECODE_TOPK), dtype=torch.int32, device=dev)
     op = torch.ops._C_ascend.npu_asu_resolve_kv_slots_single_req
+    op_lru = torch.ops.asu.npu_asu_resolve_kv_slots_lru
+    calls0 = []  # (step, context length) of every layer-0 call, replayed by the parity check
 
-    def resolve_layer(layer, topk, seq):
+    def resolve_layer(layer, topk, seq, trace_step=None):
         c = ctxs[layer]
         o0, o1 = views[layer]
+        if layer == 0:
+            calls0.append((step if trace_step is None else trace_step, seq))
+        if lru:
+            return op_lru(topk, seq, c.managed_prefix_len, c.token_state, c.asu_record_addr, c.hbm_slot_of_token,
+                          c.slot_owner_token, c.free_slot_stack, c.free_slot_count, c.lru_order, target, bt, o0, o1,
+                          c.managed_kv_cache_0, c.managed_kv_cache_1, bs, c.lru_stats)
         return op(topk, seq, c.managed_prefix_len, c.token_state, c.asu_record_addr, c.hbm_slot_of_token,
                   c.slot_owner_token, c.free_slot_stack, c.free_slot_count, bt, o0, o1, c.managed_kv_cache_0,
                   c.managed_kv_cache_1, bs)
@@ -887,11 +910,13 @@ def run_decode(args, world: int, rank: int, local_rank: int):
     # enqueue time of one step's L calls (host side), to size the pre-queued sleep
     t0 = time.perf_counter()
     for layer in range(L):
-        resolve_layer(layer, topk_dev[step - 1, layer].reshape(1, 1, -1), seq)  # all hits: state unchanged
+        # all hits (an LRU pool also refreshes their recency; the parity replay repeats it)
+        resolve_layer(layer, topk_dev[step - 1, layer].reshape(1, 1, -1), seq, trace_step=step - 1)
     torch.cuda.synchronize()
     enqueue_s = time.perf_counter() - t0
     sleep_cycles = int(min(2.0 * enqueue_s, 0.2) * 2.0e9) + 200_000
     free_before = torch.stack([c.free_slot_count for c in ctxs]).sum().item()
+    stats_before = mgr._banks[0].lru_stats.sum(0).clone() if lru else None
     ms, ms_e2e = [], []
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(gpu_index(local_rank))
@@ -909,6 +934,7 @@ def run_decode(args, world: int, rank: int, local_rank: int):
         advance()
     rank_sync(torch)
     free_mid = torch.stack([c.free_slot_count for c in ctxs]).sum().item()
+    stats_timed = (mgr._banks[0].lru_stats.sum(0) - stats_before).cpu().tolist() if lru else None
     for k in range(K):
         flush()
         torch.cuda.synchronize()
@@ -923,24 +949,36 @@ def run_decode(args, world: int, rank: int, local_rank: int):
         advance()
     rank_sync(torch)
     clock_info = clocks.stop()
-    installs_timed = free_before - free_mid
-    # parity: replay layer 0 through the oracle (states, slots, last outputs) and check the
-    # managed rows of every resident token of layer 0 against its paged-cache rows
+    # installs of the timed steps: the device counters (LRU pools) or the free-count drop
+    installs_timed = int(stats_timed[2]) if lru else free_before - free_mid
+    evictions_timed = int(stats_timed[4]) if lru else 0
+    # parity: replay every layer-0 call through the oracle (states, order, slots, last outputs)
+    # and check the managed rows of every resident token of layer 0 against its paged-cache rows
     c0 = ctxs[0]
-    ts, rec, hs, own, stack, cnt = O.reset_state(DECODE_MAX_SEQ, c0.managed_slot_count, bs, actual0, prefix,
-                                                 bt.cpu().numpy())
+    S0 = c0.managed_slot_count
+    ts, rec, hs, own, stack, cnt = O.reset_state(DECODE_MAX_SEQ, S0, bs, actual0, prefix, bt.cpu().numpy())
+    order = np.full(S0, -1, np.int32)
     src0 = np.zeros((phys * bs, 1), np.uint8)
-    dst0 = np.zeros((c0.managed_slot_count, 1), np.uint8)
-    s_ = actual0
+    dst0 = np.zeros((S0, 1), np.uint8)
     ref_out = None
-    for i in range(step):
-        ref_out = O.resolve_kv_slots_single_req(trace[i, 0].reshape(1, 1, -1), s_, ts, rec, hs, own, stack, cnt,
+    for i, s_ in calls0:
+        for t in range(actual0, s_):
+            if ts[t] == O.INVALID:
+                ts[t] = O.TAIL_HBM  # marked by mark_decode_token before this call
+        if lru:
+            ref_out, _ = O.resolve_kv_slots_lru(trace[i, 0], s_, ts, rec, hs, own, stack, cnt, order, target,
                                                 bt.cpu().numpy(), src0, src0, dst0, dst0, bs)
-        ts[s_] = O.TAIL_HBM
-        s_ += 1
+        else:
+            ref_out = O.resolve_kv_slots_single_req(trace[i, 0], s_, ts, rec, hs, own, stack, cnt, bt.cpu().numpy(),
+                                                    src0, src0, dst0, dst0, bs)
+    for t in range(actual0, seq):
+        if ts[t] == O.INVALID:
+            ts[t] = O.TAIL_HBM
+    n_res = S0 - int(cnt[0])
     if not (np.array_equal(c0.token_state.cpu().numpy(), ts) and np.array_equal(c0.hbm_slot_of_token.cpu().numpy(), hs)
             and np.array_equal(c0.slot_owner_token.cpu().numpy(), own) and int(c0.free_slot_count.item()) == int(cnt[0])
-            and np.array_equal(outs[0].cpu().numpy(), ref_out)):
+            and np.array_equal(outs[0].cpu().numpy().reshape(-1), ref_out.reshape(-1))
+            and (not lru or np.array_equal(c0.lru_order.cpu().numpy()[:n_res], order[:n_res]))):
         raise RuntimeError("decode resolver state differs from the oracle")
     resident = torch.nonzero(c0.token_state == O.HBM_RESIDENT).reshape(-1)
     paged = bt.reshape(-1).long()[resident // bs] * bs + resident % bs
@@ -956,16 +994,18 @@ def run_decode(args, world: int, rank: int, local_rank: int):
     calls, cpu_s = 0, 0.0
     if not args.no_cpu_baseline:
         calls, cpu_s = decode_cpu_leg(trace, bt.cpu().numpy(), actual0, prefix, c0.managed_slot_count, phys * bs,
-                                      base, K, args.cpu_sample_s)
+                                      base, K, args.cpu_sample_s, free_target=target)
     idx = world * L * DECODE_TOPK * K
     p50 = statistics.median(ms)
     value = idx / (tot_ms * 1e-3)
     line = base_line(world, K, args.warmup, tot_ms / K, value,
-                     {"workload": f"decode: 1 request/GPU, {L} layers x npu_asu_resolve_kv_slots_single_req, "
+                     {"workload": f"{args.workload}: 1 request/GPU, {L} layers x "
+                                  f"{'npu_asu_resolve_kv_slots_lru' if lru else 'npu_asu_resolve_kv_slots_single_req'}, "
                                   f"max_seq {DECODE_MAX_SEQ}, context {actual0}..{actual0 + n_steps} "
                                   f"(ASU prefix {prefix}), top-k {DECODE_TOPK} (70% reuse + zipf 1.1, newest "
                                   f"token included), bf16 rows {DECODE_ROW0}+{DECODE_ROW1}, block {bs}, "
-                                  f"{c0.managed_slot_count} managed slots/layer", "l2": L2_NOTE})
+                                  f"{c0.managed_slot_count} managed slots/layer"
+                                  + (f" (exact LRU, free target {target})" if lru else ""), "l2": L2_NOTE})
     hbm = float(load_peaks().get("hbm_gbs", 6650.0))
     per_inst = 2 * (2 * DECODE_ROW0 + 2 * DECODE_ROW1) + 4 * 6
     alg = (installs_timed / K) * per_inst + L * DECODE_TOPK * 16
@@ -973,9 +1013,13 @@ def run_decode(args, world: int, rank: int, local_rank: int):
     line.update({
         "p50_step_us": p50 * 1e3, "p50_call_us": p50 * 1e3 / L,
         "installs_per_step": installs_timed / K, "miss_rate": installs_timed / (K * L * DECODE_TOPK),
-        "roofline": {"bound": "hbm", "kernel": "resolve_kernel (per layer; DSA / MLA rows copied by the cluster)",
+        "evictions_per_step": evictions_timed / K,
+        "host_enqueue_us_per_call": enqueue_s / L * 1e6,
+        "copied_bytes_per_step": installs_timed / K * 2 * (DECODE_ROW0 + DECODE_ROW1),
+        "roofline": {"bound": "hbm", "kernel": ("resolve_lru_kernel (per layer; rows copied by the CTA)" if lru else
+                                                 "resolve_kernel (per layer; DSA / MLA rows copied by the cluster)"),
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "traffic": RESOLVE_DRAM_BYTES_PER_CALL * L,
+                     "traffic": None if lru else RESOLVE_DRAM_BYTES_PER_CALL * L,
                      "traffic_kind": "resolve_kernel dram__bytes_read + write per call (ncu, 4-layer case) x layers",
                      "algorithmic_bytes_per_step": alg,
                      "note": "latency-bound: one 8-CTA cluster resolves a 2048-entry top-k; bytes per step are small"},
@@ -1304,7 +1348,7 @@ def main():
             run_resolver(args, RESOLVER_WORKLOADS[args.workload], world, rank, local_rank)
         elif args.workload == "lru1":
             run_lru1(args, world, rank, local_rank)
-        elif args.workload == "decode":
+        elif args.workload in ("decode", "decode-lru"):
             run_decode(args, world, rank, local_rank)
         elif args.workload == "writeback":
             run_writeback(args, world, rank, local_rank)

@@ -262,6 +262,53 @@ int asu_resolver_reset(void* stream, int32_t* token_state, int32_t* asu_record_a
                        int64_t block_table_len, int64_t block_size, int64_t actual_seq_len,
                        int64_t managed_prefix_len);
 
+/* The resolver over a bounded managed pool: asu_kv_resolver_do's token-state machine fused with
+ * exact-LRU eviction, for a managed cache smaller than the context (e.g. 8192 resident + 2048
+ * free slots at a 128K-token context).  No single reference function: it composes the resolver
+ * (patch/0001 asu_kv_resolver.py, patch lines 954-1039), which raises "free_slot_stack does not
+ * have enough slots" (patch lines 879-888) once the pool is full, with LRUManagedCache
+ * (simu/kv_cache_eviction_sim.py:124-150):
+ *   1. while free_slot_count < min(free_target, slot_count) and slots are resident, the least
+ *      recently used slot (lru_order[0]) is evicted: its token returns to ASU_ONLY when
+ *      asu_record_addr[tok] >= 0, else TAIL_HBM; hbm_slot_of_token[tok] and the slot's owner
+ *      become INVALID; the slot is pushed on free_slot_stack;
+ *   2. topk is resolved in order as by asu_kv_resolver_do, hits moving their slot to the most
+ *      recently used end and installs entering there.
+ * lru_order [slot_count] int32: the first slot_count - free_slot_count entries are the resident
+ * slots, least recently used first (after asu_resolver_reset: none).  free_slot_stack,
+ * slot_owner_token and lru_order all hold slot_count entries.  Limits: topk_numel <= 4096,
+ * slot_count <= 16384, kv0_row_bytes + kv1_row_bytes <= 1 MiB; one launch, no workspace.
+ * Differences from the reference on bad input: an entry whose source row is out of range sets
+ * ASU_ST_BAD_SOURCE and takes no slot; no free slot left sets ASU_ST_FREE_EXHAUSTED (slot -1).
+ * evicted (>= min(free_target, slot_count) entries) / evicted_count: the evicted tokens in
+ * eviction order (both nullable); stats: ASU_LRU_STAT_COLS int64, += (nullable); status: one
+ * int32 (nullable). */
+int asu_kv_resolver_lru(void* stream, const int32_t* topk, int64_t topk_numel, int32_t* token_state,
+                        const int32_t* asu_record_addr, int32_t* hbm_slot_of_token, int32_t* slot_owner_token,
+                        int32_t* free_slot_stack, int32_t* free_slot_count, int32_t* lru_order, int64_t slot_count,
+                        int64_t free_target, const int32_t* block_table, int64_t block_table_len, const void* kv0_src,
+                        const void* kv1_src, void* kv0_dst, void* kv1_dst, int64_t kv0_row_bytes,
+                        int64_t kv1_row_bytes, int64_t src_rows, int64_t max_seq_len, int64_t actual_seq_len,
+                        int64_t block_size, int32_t* resolved, int32_t* evicted, int32_t* evicted_count,
+                        int64_t* stats, int32_t* status);
+
+/* asu_resolver_reset for `layers` layers in one launch: token_state / asu_record_addr /
+ * hbm_slot_of_token are [layers, max_seq_len], slot_owner_token / free_slot_stack are
+ * [layers, slot_count] and free_slot_count is [layers], all contiguous; every layer gets the same
+ * reset (one request, one block table).  The reference resets layer by layer (patch/0003
+ * ASUFullKVCacheManagerFunctional.reset_single_request, patch lines 411-426). */
+int asu_resolver_reset_layers(void* stream, int64_t layers, int32_t* token_state, int32_t* asu_record_addr,
+                              int32_t* hbm_slot_of_token, int64_t max_seq_len, int32_t* slot_owner_token,
+                              int32_t* free_slot_stack, int32_t* free_slot_count, int64_t slot_count,
+                              const int32_t* block_table, int64_t block_table_len, int64_t block_size,
+                              int64_t actual_seq_len, int64_t managed_prefix_len);
+
+/* Replaces ASUFullKVCacheManagerFunctional.mark_decode_token (patch/0003, patch lines 294-298 and
+ * 428-432: token_state[token_id] = TAIL_HBM in every layer) with one launch over a
+ * [layers, max_seq_len] token_state.  Rejects token_id outside [0, max_seq_len). */
+int asu_resolver_mark_token(void* stream, int64_t layers, int32_t* token_state, int64_t max_seq_len,
+                            int64_t token_id);
+
 /* No counterpart in the reference.  The same resolver as asu_kv_resolver_do, for callers that
  * cannot allocate device memory while resolving (an engine whose HBM is pre-reserved for its
  * KV-block pool and that forbids cudaMalloc in the decode loop; a C / FFI host without a

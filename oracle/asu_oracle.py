@@ -413,6 +413,56 @@ def reset_state(max_seq_len, slot_count, block_size, actual_seq_len, managed_pre
     return token_state, record, hbm_slot, owner, stack, count
 
 
+def resolve_kv_slots_lru(topk, actual_seq_len, token_state, asu_record_addr, hbm_slot_of_token, slot_owner_token,
+                         free_slot_stack, free_slot_count, lru_order, free_target, block_table,
+                         kv0_src, kv1_src, kv0_dst, kv1_dst, block_size):
+    """The resolver over a bounded managed pool: the exact LRU pool of
+    simu/kv_cache_eviction_sim.py (LRUManagedCache, :124-150) composed with the resolver of
+    patch/0001 (asu_resolve_kv_slots_single_req, patch lines 954-1039).
+
+    The resident slots are ``lru_order[: S - free_slot_count]``, least recently used first.
+    1. Step-boundary maintain (prepare_free_slots, :124-131): while the free count is below
+       ``min(free_target, S)`` and slots are resident, the LRU slot is evicted.  Its token goes
+       back to ASU_ONLY when it has a record address (a prefix token read from the ASU store),
+       else to TAIL_HBM (read from the paged cache again); its hbm_slot_of_token and the slot's
+       owner are cleared and the slot is pushed on the free stack.
+    2. Resolve (resolve_query, :133-150, with the resolver's install): an HBM_RESIDENT token is a
+       hit and its slot becomes the most recently used; an ASU_ONLY / TAIL_HBM token is installed
+       exactly as the resolver installs it (pop the stack top, copy the row pair, mark it
+       resident), its slot the most recently used.  Errors raise ResolverError where the
+       resolver raises.
+    Mutates every state array in place; returns (resolved slots with topk's shape, evicted
+    tokens in eviction order).
+    """
+    slots = int(slot_owner_token.shape[0])
+    resident = slots - int(free_slot_count[0])
+    order = OrderedDict((int(s), None) for s in lru_order[:resident])
+    evicted = []
+    while int(free_slot_count[0]) < min(int(free_target), slots) and order:
+        victim, _ = order.popitem(last=False)
+        tok = int(slot_owner_token[victim])
+        if 0 <= tok < token_state.shape[0]:
+            token_state[tok] = ASU_ONLY if int(asu_record_addr[tok]) >= 0 else TAIL_HBM
+            hbm_slot_of_token[tok] = INVALID
+        slot_owner_token[victim] = INVALID
+        free_slot_stack[int(free_slot_count[0])] = victim
+        free_slot_count[0] += 1
+        evicted.append(tok)
+    flat = np.asarray(topk).reshape(-1)
+    out = np.empty(flat.shape, np.int32)
+    for i, tok in enumerate(flat):
+        # the resolver's per-token semantics, one token at a time, then the touch
+        slot = int(resolve_kv_slots_single_req(
+            np.array([tok], np.int32), actual_seq_len, token_state, asu_record_addr, hbm_slot_of_token,
+            slot_owner_token, free_slot_stack, free_slot_count, block_table, kv0_src, kv1_src, kv0_dst, kv1_dst,
+            block_size)[0])
+        order[slot] = None
+        order.move_to_end(slot)
+        out[i] = slot
+    lru_order[: len(order)] = np.fromiter(order.keys(), np.int32, len(order))
+    return out.reshape(np.asarray(topk).shape), np.asarray(evicted, np.int32)
+
+
 # ---------------------------------------------------------------------------
 # Swap-in gather: host row pool -> HBM slot pool (byte copy)
 # ---------------------------------------------------------------------------

@@ -192,3 +192,104 @@ def test_decode_flow_at_full_context_against_oracle():
         mgr.mark_decode_token(seq)
         ts[seq] = O.TAIL_HBM
         seq += 1
+
+
+def test_batched_reset_and_mark_cover_every_layer_and_only_the_layer_asked():
+    """The manager keeps every layer's state in one [layers, ...] bank: a request reset is one
+    launch for all 61 layers and equals the reference reset in each; a decode token is marked in
+    all layers at once; a context's own reset_state / mark_decode_token touch its layer only."""
+    import asu_ascend_b200
+
+    asu_ascend_b200.load()
+    from asu_ascend_b200 import manager as M
+
+    max_seq, bs, slots = 4096, 64, 1024
+    nblk = max_seq // bs
+    rng = np.random.Generator(np.random.PCG64(61))
+    bt = rng.permutation(nblk + 4)[:nblk].astype(np.int32)
+    caches = {f"layers.{i}.attn": (torch.zeros((nblk + 4, bs, 1, 8), dtype=torch.bfloat16, device=DEV),
+                                   torch.zeros((nblk + 4, bs, 1, 4), dtype=torch.bfloat16, device=DEV))
+              for i in range(61)}
+    mgr = M.ASUFullKVCacheManagerFunctional.from_kv_caches(caches, max_seq, bs, managed_slot_count=slots,
+                                                           enabled=True)
+    ctxs = [mgr.get_layer_context(f"layers.{i}.attn") for i in range(61)]
+    for c in ctxs:  # dirty every layer first
+        c.token_state.fill_(7)
+        c.free_slot_count.fill_(3)
+        c.free_slot_stack.fill_(9)
+    mgr.reset_single_request("req", 4000, 3990, torch.from_numpy(bt[None, :]))
+    ts, rec, hs, own, stack, cnt = O.reset_state(max_seq, slots, bs, 4000, 3990, bt)
+    for c in ctxs:
+        np.testing.assert_array_equal(c.token_state.cpu().numpy(), ts)
+        np.testing.assert_array_equal(c.asu_record_addr.cpu().numpy(), rec)
+        np.testing.assert_array_equal(c.hbm_slot_of_token.cpu().numpy(), hs)
+        np.testing.assert_array_equal(c.slot_owner_token.cpu().numpy(), own)
+        np.testing.assert_array_equal(c.free_slot_stack.cpu().numpy(), stack)
+        assert int(c.free_slot_count.item()) == slots
+        assert (c.req_id, c.actual_seq_len, c.managed_prefix_len) == ("req", 4000, 3990)
+    mgr.mark_decode_token(4000)
+    assert all(int(c.token_state[4000].item()) == M.TAIL_HBM and c.actual_seq_len == 4001 for c in ctxs)
+    ctxs[5].mark_decode_token(4001)
+    assert [int(c.token_state[4001].item()) for c in ctxs].count(M.TAIL_HBM) == 1
+    assert ctxs[5].actual_seq_len == 4002 and ctxs[6].actual_seq_len == 4001
+    ctxs[7].token_state.fill_(7)
+    ctxs[7].reset_state("other", 100, 50, torch.from_numpy(bt[None, :]))
+    assert ctxs[7].req_id == "other" and ctxs[8].req_id == "req"
+    assert int(ctxs[8].token_state[4000].item()) == M.TAIL_HBM
+    ts7, rec7, *_ = O.reset_state(max_seq, slots, bs, 100, 50, bt)
+    np.testing.assert_array_equal(ctxs[7].token_state.cpu().numpy(), ts7)
+    np.testing.assert_array_equal(ctxs[7].asu_record_addr.cpu().numpy(), rec7)
+
+
+def test_bounded_pool_decode_flow_at_full_context_against_oracle():
+    """The decode workload's context over an exact-LRU pool of 8192 + 2048 slots (free target
+    2048) through the manager and sparse_mla.resolve_topk: reset, twelve decode steps with a
+    marked decode token each (the pool fills and then evicts), every state array, the recency
+    order and every managed row against the oracle (the resolver composed with the LRU pool)."""
+    import asu_ascend_b200
+
+    asu_ascend_b200.load()
+    from asu_ascend_b200 import sparse_mla as S
+
+    rng = np.random.Generator(np.random.PCG64(22))
+    max_seq, bs, slots, target = 131072, 64, 10240, 2048
+    actual, prefix = 131000, 130944
+    nblk = max_seq // bs
+    bt = rng.permutation(nblk + 16)[:nblk].astype(np.int32)
+    kv = torch.randint(0, 256, (nblk + 16, bs, 656), dtype=torch.uint8, device=DEV)
+    mgr = S.contexts_for_mla({"l": kv}, max_seq, bs, managed_slot_count=slots, enabled=True, free_target=target)
+    ctx = mgr.get_layer_context("l")
+    assert ctx.bounded
+    ctx.managed_kv_cache_0.zero_()
+    gbt = torch.from_numpy(bt).to(DEV)
+    mgr.reset_single_request("r", actual, prefix, gbt[None, :])
+    ts, rec, hs, own, stack, cnt = O.reset_state(max_seq, slots, bs, actual, prefix, bt)
+    order = np.full(slots, -1, np.int32)
+    src = kv.view(-1, 656).cpu().numpy()
+    dst = np.zeros((slots, 656), np.uint8)
+    e_src, e_dst = np.zeros((src.shape[0], 0), np.uint8), np.zeros((slots, 0), np.uint8)
+    seq = actual
+    hot = rng.integers(0, seq, 40000)
+    prev = rng.choice(hot, 2048)
+    for step in range(12):
+        q = np.where(rng.random(2048) < 0.5, prev, rng.choice(hot, 2048)).astype(np.int32)
+        q[-1] = seq - 1
+        prev = q
+        exp, _ = O.resolve_kv_slots_lru(q, seq, ts, rec, hs, own, stack, cnt, order, target, bt, src, e_src, dst,
+                                        e_dst, bs)
+        out = S.resolve_topk(ctx, torch.from_numpy(q[None, :]).to(DEV), gbt, kv)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.cpu().numpy()[0], exp, err_msg=f"step {step}")
+        np.testing.assert_array_equal(ctx.token_state.cpu().numpy(), ts)
+        np.testing.assert_array_equal(ctx.hbm_slot_of_token.cpu().numpy(), hs)
+        np.testing.assert_array_equal(ctx.slot_owner_token.cpu().numpy(), own)
+        c = int(cnt[0])
+        assert int(ctx.free_slot_count.item()) == c
+        np.testing.assert_array_equal(ctx.lru_order.cpu().numpy()[: slots - c], order[: slots - c])
+        np.testing.assert_array_equal(ctx.managed_kv_cache_0[:slots].cpu().numpy(), dst)
+        mgr.mark_decode_token(seq)
+        ts[seq] = O.TAIL_HBM
+        seq += 1
+    assert (own >= 0).sum() == slots - c
+    hits, misses, installs, shortages, evictions = ctx.lru_stats.tolist()
+    assert evictions > 0 and shortages == 0 and installs == misses and hits + misses == 12 * 2048

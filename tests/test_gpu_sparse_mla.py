@@ -102,11 +102,17 @@ def _impl(cls, heads, scale, topk_buffer):
     return impl
 
 
-@pytest.mark.parametrize("heads", [16, 128])
-def test_vllm_subclass_decode_steps_match_stock_flashmla_sparse(heads):
-    """Three decode steps of one request through ASUFlashMLASparseImpl.forward_mqa: each step's
-    output equals vLLM's own FlashMLASparseImpl over the paged cache, the first step resets the
-    manager, the next ones mark the new decode token, and a shared manager serves two layers."""
+# managed pools: one slot per context position (never evicts, the reference's setting), or an
+# exact-LRU pool of 2560 slots keeping 2048 free over an 8000-token context (evicts every step)
+POOLS = {"full": (None, None, 3000), "lru": (2560, 2048, 8000)}
+
+
+@pytest.mark.parametrize("heads,pool", [(16, "full"), (128, "full"), (16, "lru"), (128, "lru")])
+def test_vllm_subclass_decode_steps_match_stock_flashmla_sparse(heads, pool):
+    """Decode steps of one request through ASUFlashMLASparseImpl.forward_mqa: each step's output
+    equals vLLM's own FlashMLASparseImpl over the paged cache, the first step resets the manager,
+    the next ones mark the new decode token, and a shared manager serves two layers -- over a pool
+    with a slot per context position and over an exact-LRU pool smaller than the context."""
     pytest.importorskip("vllm.third_party.flashmla.flash_mla_interface")
     from types import SimpleNamespace
 
@@ -115,12 +121,14 @@ def test_vllm_subclass_decode_steps_match_stock_flashmla_sparse(heads):
     from asu_ascend_b200 import sparse_mla as S
     from asu_ascend_b200 import vllm_backend as V
 
-    seq0, steps, bs, scale = 3000, 3, 64, 576 ** -0.5
+    slots, target, seq0 = POOLS[pool]
+    steps, bs, scale = (3 if target is None else 5), 64, 576 ** -0.5
     kv, bt, _ = _case(11, seq0 + steps, tokens=1)
     kv2 = kv.flip(0).contiguous()  # a second layer's cache
     g = torch.Generator().manual_seed(12)
     mgr = S.contexts_for_mla({"layers.0.attn": kv, "layers.1.attn": kv2}, max_seq_len=seq0 + steps, block_size=bs,
-                             managed_slot_count=seq0 + steps, enabled=True)
+                             managed_slot_count=slots or seq0 + steps, enabled=True, free_target=target)
+    assert mgr.get_layer_context("layers.0.attn").bounded == (target is not None)
     buf = torch.full((1, 2048), -1, dtype=torch.int32, device=DEV)
     asu = _impl(V.asu_flashmla_sparse_impl(), heads, scale, buf)
     stock = _impl(FlashMLASparseImpl, heads, scale, buf)
@@ -130,7 +138,7 @@ def test_vllm_subclass_decode_steps_match_stock_flashmla_sparse(heads):
                              block_table=bt.view(1, -1), req_id_per_token=torch.zeros(1, dtype=torch.int32, device=DEV),
                              block_size=bs, asu_kv_cache_manager=mgr, asu_req_id="req-0")
         topk = torch.full((2048,), -1, dtype=torch.int32)
-        k = 1900 + 40 * step
+        k = 1900 + 30 * step
         topk[:k] = torch.randperm(seq, generator=g)[:k].to(torch.int32)
         topk[0] = seq - 1  # the token this step decodes
         buf[0].copy_(topk)
@@ -142,6 +150,8 @@ def test_vllm_subclass_decode_steps_match_stock_flashmla_sparse(heads):
             torch.testing.assert_close(got.float(), exp.float(), rtol=2e-2, atol=2e-2)
         ctx = mgr.get_layer_context("layers.1.attn")
         assert (ctx.req_id, ctx.actual_seq_len, ctx.managed_prefix_len) == ("req-0", seq, seq0 - 1)
+    if target is not None:  # the pool did evict, and every layer keeps `target` slots free at each call
+        assert int(ctx.free_slot_count.item()) < target
 
 
 def _fp8_ds_mla_cache(seed, blocks, bs=64):
@@ -154,11 +164,13 @@ def _fp8_ds_mla_cache(seed, blocks, bs=64):
     return torch.cat([nope, scales, rope], 1).view(blocks, bs, 656).to(DEV)
 
 
-@pytest.mark.parametrize("layout", ["mixed", "separate"])
-def test_vllm_subclass_fp8_decode_matches_stock_flashmla(layout):
+@pytest.mark.parametrize("layout,pool", [("mixed", "full"), ("separate", "full"), ("mixed", "lru"),
+                                         ("separate", "lru")])
+def test_vllm_subclass_fp8_decode_matches_stock_flashmla(layout, pool):
     """fp8_ds_mla caches: the subclass decodes with FlashMLA's fp8 sparse decode over the managed
-    pages; each of three steps equals vLLM's stock FlashMLASparseImpl (same kernel over the paged
-    cache) in both fp8 batch layouts, with a managed pool that is not a whole number of pages."""
+    pages; each step equals vLLM's stock FlashMLASparseImpl (same kernel over the paged cache) in
+    both fp8 batch layouts, with a managed pool that is not a whole number of pages (one slot per
+    context position) and with an exact-LRU pool smaller than the context."""
     fi = pytest.importorskip("vllm.third_party.flashmla.flash_mla_interface")
     from types import SimpleNamespace
 
@@ -167,13 +179,15 @@ def test_vllm_subclass_fp8_decode_matches_stock_flashmla(layout):
     from asu_ascend_b200 import sparse_mla as S
     from asu_ascend_b200 import vllm_backend as V
 
-    seq0, steps, bs, heads, scale = 2500, 3, 64, 16, 576 ** -0.5
+    slots, target, seq0 = POOLS[pool]
+    seq0 = 2500 if target is None else seq0
+    steps, bs, heads, scale = (3 if target is None else 5), 64, 16, 576 ** -0.5
     nblk = (seq0 + steps + bs - 1) // bs
     kv = _fp8_ds_mla_cache(21, nblk + 5)
     g = torch.Generator().manual_seed(22)
     bt = torch.randperm(nblk + 5, generator=g)[:nblk].to(torch.int32).to(DEV)
     mgr = S.contexts_for_mla({"layers.0.attn": kv}, max_seq_len=seq0 + steps, block_size=bs,
-                             managed_slot_count=seq0 + steps, enabled=True)
+                             managed_slot_count=slots or seq0 + steps, enabled=True, free_target=target)
     assert mgr.get_layer_context("layers.0.attn").managed_kv_cache_0.shape[0] % bs == 0
     buf = torch.full((1, 2048), -1, dtype=torch.int32, device=DEV)
     impls = []
@@ -198,7 +212,7 @@ def test_vllm_subclass_fp8_decode_matches_stock_flashmla(layout):
     for step in range(steps):
         seq = seq0 + step
         topk = torch.full((2048,), -1, dtype=torch.int32)
-        k = 1800 + 50 * step
+        k = 1800 + 40 * step
         topk[:k] = torch.randperm(seq, generator=g)[:k].to(torch.int32)
         topk[0] = seq - 1
         buf[0].copy_(topk)
