@@ -59,6 +59,13 @@ _SIGS = {
                      c_uint32, c_uint32],
     "asu_swapin_gather": [_P, _P, c_int64, c_uint32, c_uint32, _P, c_uint32, _P, _P, _P, c_uint32, _P, c_uint32,
                           c_uint32, _P],
+    "asu_swapin_gather_to_peer": [_P, _P, c_int64, c_uint32, c_uint32, _P, c_uint32, _P, _P, _P, c_uint32, _P,
+                                  c_uint32, c_uint32, _P],
+    "asu_host_register": [_P, c_uint64, POINTER(c_void_p)],
+    "asu_host_unregister": [_P],
+    "asu_ipc_export": [_P, _P, POINTER(c_uint64)],
+    "asu_ipc_open": [_P, POINTER(c_void_p)],
+    "asu_ipc_close": [_P],
     "asu_host_pool_alloc": [c_uint64, POINTER(c_void_p), POINTER(c_void_p)],
     "asu_host_pool_writeback": [_P, _P, c_int64, c_uint32, c_uint32, _P, c_int64, c_uint64, _P, _P, c_int64, _P],
     "asu_host_pool_free": [_P],

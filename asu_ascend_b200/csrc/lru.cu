@@ -60,13 +60,17 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
     const uint32_t H = 1u << log2h;
     const uint32_t Sp = (S + 3) & ~3u;  // row length rounded up to 16 bytes
     int32_t* s_order = smem;            // [Sp] old order row, later the new one
-    int32_t* s_last = s_order + Sp;     // [Sp] last touching position, -1 untouched, -2 victim
+    int32_t* s_last = s_order + Sp;     // [Sp] last touching position (-1 untouched, -2 victim)
     int32_t* s_hkey = s_last + Sp;      // [H]  hash: key
-    int32_t* s_hpos = s_hkey + H;      // [H]  hash: first position
-    int32_t* s_hval = s_hpos + H;      // [H]  hash: installed slot
+    int32_t* s_hpos = s_hkey + H;       // [H]  hash: first position of the key
+    int32_t* s_hmax = s_hpos + H;       // [H]  hash: last position of the key
+    int32_t* s_hval = s_hmax + H;       // [H]  hash: installed slot
     __shared__ int scan_a[32], scan_b[32];  // alternating buffers of the one-barrier block scans
     __shared__ int n_hits, n_valid;
     const int tid = threadIdx.x;
+    // victims held in registers per thread (positions tid + i * kThreads); more than
+    // kVict * kThreads victims (a free target above 4096) are unmapped at once in P0
+    constexpr int kVict = IPT_S < 4 ? IPT_S : 4;
 
     for (uint32_t r = blockIdx.x; r < req_num; r += gridDim.x) {
         int32_t* trow = t2s + static_cast<uint64_t>(r) * K;
@@ -76,24 +80,24 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
         const int32_t* qrow = query + static_cast<uint64_t>(r) * Q;
         int32_t bits = 0;
 
-        // ---- P0: issue every independent load ----
+        // ---- P0: loads, shared-memory set-up and the eviction's marks, one phase ----
+        // Every independent load is issued first: the free count, the order row (16-byte loads
+        // into registers), the queries and their token_to_slot gathers.  The victims are the head
+        // of the order row, lru_order[0, E), E = min(target - free, residents); each thread loads
+        // its victim entries itself as soon as the count is in, marks them in shared memory
+        // (last_pos = -2, so a query that reads a victim's slot is classified as a miss -- the
+        // serial evict-then-resolve order) and loads their keys, which the unmapping after the
+        // classification consumes.  Residents that survive get last_pos = -1 from the thread that
+        // loaded their order entry; free slots get theirs when they are popped.
         const int32_t free0 = ld_cg(count + r);
         const bool vec_row = (S % 4 == 0) && (reinterpret_cast<uintptr_t>(orow) % 16 == 0);
+        constexpr int kVec = (IPT_S + 3) / 4;
+        int4 ov[kVec];
         if (vec_row) {
-            // all of a thread's row loads in flight before the first shared-memory store
-            // (S <= IPT_S * kThreads, so IPT_S / 4 16-byte loads per thread cover the row)
-            constexpr int kVec = (IPT_S + 3) / 4;
             const int4* src = reinterpret_cast<const int4*>(orow);
-            int4* dst = reinterpret_cast<int4*>(s_order);
-            int4 ov[kVec];
 #pragma unroll
             for (int j = 0; j < kVec; ++j)
                 if (tid + j * kThreads < S / 4) ov[j] = __ldcg(src + tid + j * kThreads);
-#pragma unroll
-            for (int j = 0; j < kVec; ++j)
-                if (tid + j * kThreads < S / 4) dst[tid + j * kThreads] = ov[j];
-        } else {
-            for (uint32_t i = tid; i < S; i += kThreads) s_order[i] = ld_cg(orow + i);
         }
         int32_t key[IPT_Q], g[IPT_Q];
 #pragma unroll
@@ -108,14 +112,11 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
         }
         {
             const int4 m1 = make_int4(-1, -1, -1, -1);
-            // S4 and H are multiples of 4 elements of 16-byte aligned arrays (S4 rounds S up
-            // inside the dynamic allocation, see lru_smem_bytes)
-            const uint32_t S4 = (S + 3) / 4;
-            for (uint32_t i = tid; i < S4; i += kThreads) reinterpret_cast<int4*>(s_last)[i] = m1;
             const int4 big = make_int4(INT32_MAX, INT32_MAX, INT32_MAX, INT32_MAX);
             for (uint32_t i = tid; i < H / 4; i += kThreads) {
                 reinterpret_cast<int4*>(s_hkey)[i] = m1;
                 reinterpret_cast<int4*>(s_hpos)[i] = big;
+                reinterpret_cast<int4*>(s_hmax)[i] = m1;
             }
         }
         if (tid == 0) {
@@ -132,49 +133,65 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
         int32_t E = 0;
         if (free0 < tgt) E = (tgt - free0) < resident0 ? (tgt - free0) : resident0;
         const int32_t free1 = free0 + E;
-        __syncthreads();
 
-        // ---- P1: eviction of lru_order[0, E): mark the victims now, load their keys; the
-        // unmapping stores follow the classification, so the loads overlap it ----
-        // (with more than 8 slots per thread the keys would not stay in registers: those
-        // configurations unmap the victims right here instead)
-        constexpr bool kDeferUnmap = IPT_S <= 8;
-        constexpr int kVict = kDeferUnmap ? IPT_S : 1;
         int32_t vslot[kVict], vkey[kVict];
-        if constexpr (kDeferUnmap) {
 #pragma unroll
-            for (int i = 0; i < IPT_S; ++i) {
-                const int32_t k = tid + i * kThreads;
-                vslot[i] = k < E ? s_order[k] : kNotFound;
-                vkey[i] = kNotFound;
-                if (k < E) {
-                    if (static_cast<uint32_t>(vslot[i]) < S) {
-                        s_last[vslot[i]] = kVictim;
-                        vkey[i] = ld_cg(srow + vslot[i]);
-                    } else {
-                        bits |= ASU_ST_BAD_STATE;
-                    }
+        for (int i = 0; i < kVict; ++i) {
+            const int32_t k = tid + i * kThreads;
+            vslot[i] = k < E ? ld_cg(orow + k) : kNotFound;
+        }
+        // the order row into shared memory; last_pos of the surviving residents
+        if (vec_row) {
+            int4* dst = reinterpret_cast<int4*>(s_order);
+#pragma unroll
+            for (int j = 0; j < kVec; ++j) {
+                const int32_t i4 = tid + j * kThreads;
+                if (i4 >= static_cast<int32_t>(S / 4)) continue;
+                dst[i4] = ov[j];
+                const int32_t v[4] = {ov[j].x, ov[j].y, ov[j].z, ov[j].w};
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const int32_t k = 4 * i4 + c;
+                    if (k >= E && k < resident0 && static_cast<uint32_t>(v[c]) < S) s_last[v[c]] = -1;
                 }
             }
         } else {
-            for (int32_t k = tid; k < E; k += kThreads) {
-                const int32_t v = s_order[k];
-                int32_t vk = kNotFound;
-                if (static_cast<uint32_t>(v) < S) {
-                    s_last[v] = kVictim;
-                    vk = ld_cg(srow + v);
-                    if (static_cast<uint32_t>(vk) < K) st_cg(trow + vk, kNotFound);
-                    else bits |= ASU_ST_BAD_STATE;
-                    st_cg(srow + v, kNotFound);
-                    st_cg(krow + free0 + k, v);
-                } else {
-                    bits |= ASU_ST_BAD_STATE;
-                }
-                if (static_cast<uint32_t>(k) < ev_stride) evicted[static_cast<uint64_t>(r) * ev_stride + k] = vk;
+            for (int32_t k = tid; k < static_cast<int32_t>(S); k += kThreads) {
+                const int32_t v = ld_cg(orow + k);
+                s_order[k] = v;
+                if (k >= E && k < resident0 && static_cast<uint32_t>(v) < S) s_last[v] = -1;
             }
         }
+#pragma unroll
+        for (int i = 0; i < kVict; ++i) {
+            vkey[i] = kNotFound;
+            if (tid + i * kThreads >= E) continue;
+            if (static_cast<uint32_t>(vslot[i]) < S) {
+                s_last[vslot[i]] = kVictim;
+                vkey[i] = ld_cg(srow + vslot[i]);
+            } else {
+                bits |= ASU_ST_BAD_STATE;
+            }
+        }
+        // victims beyond the registers: marked and unmapped here (a racing gather of such a key
+        // reads either the victim slot, marked, or -1: a miss either way)
+        for (int32_t k = tid + kVict * kThreads; k < E; k += kThreads) {
+            const int32_t v = ld_cg(orow + k);
+            int32_t vk = kNotFound;
+            if (static_cast<uint32_t>(v) < S) {
+                s_last[v] = kVictim;
+                vk = ld_cg(srow + v);
+                if (static_cast<uint32_t>(vk) < K) st_cg(trow + vk, kNotFound);
+                else bits |= ASU_ST_BAD_STATE;
+                st_cg(srow + v, kNotFound);
+                st_cg(krow + free0 + k, v);
+            } else {
+                bits |= ASU_ST_BAD_STATE;
+            }
+            if (static_cast<uint32_t>(k) < ev_stride) evicted[static_cast<uint64_t>(r) * ev_stride + k] = vk;
+        }
         if (tid == 0) ev_count[r] = E;
-        __syncthreads();  // victim marks visible
+        __syncthreads();  // order row, marks and hash set up
 
         // ---- P2: classify; hits record their position, misses enter the hash ----
         uint8_t st[IPT_Q];
@@ -204,15 +221,16 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
                     h = (h + 1) & (H - 1);
                 }
                 hidx[j] = static_cast<int32_t>(h);
-                atomicMin(&s_hpos[h], pos);  // the first position of the key wins
+                atomicMin(&s_hpos[h], pos);  // the first position of the key installs
+                atomicMax(&s_hmax[h], pos);  // the last one is its slot's last touch
             } else {
                 st[j] = kBad;
                 bits |= ASU_ST_BAD_STATE;
             }
         }
-        // victim unmapping (P1's stores), ordered before any install by the barrier below
+        // victim unmapping, ordered before any install by the barrier below
 #pragma unroll
-        for (int i = 0; i < (kDeferUnmap ? IPT_S : 0); ++i) {
+        for (int i = 0; i < kVict; ++i) {
             const int32_t k = tid + i * kThreads;
             if (k >= E) continue;
             const int32_t v = vslot[i];
@@ -243,7 +261,6 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
             slot[j] = st[j] == kHit ? g[j] : kNotFound;
             inst[j] = 0;
             if (!canon[j]) continue;
-            const int32_t pos = tid * IPT_Q + j;
             const int32_t k = rank++;
             int32_t s = kNotFound;
             if (k < free1) {
@@ -259,7 +276,8 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
             if (s >= 0) {
                 st_cg(trow + key[j], s);
                 st_cg(srow + s, key[j]);
-                atomicMax(&s_last[s], pos);
+                // only this thread touches a popped slot before the next barrier
+                s_last[s] = s_hmax[hidx[j]];
                 inst[j] = 1;
             } else {
                 bits |= ASU_ST_SHORTAGE;
@@ -268,9 +286,9 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
         }
         const int32_t n_inst = n_canon < free1 ? n_canon : free1;
         const int32_t free2 = free1 - n_inst;
-        __syncthreads();
+        __syncthreads();  // installed slots and their last touches visible
 
-        // ---- P4: later duplicates of a missing key, outputs ----
+        // ---- P4: later duplicates of a missing key read its slot; outputs ----
         int hits_local = 0;
 #pragma unroll
         for (int j = 0; j < IPT_Q; ++j) {
@@ -281,7 +299,6 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
                 if (v >= 0) {
                     slot[j] = v;
                     hit = true;
-                    atomicMax(&s_last[v], pos);
                 }
             }
             hits_local += hit;
@@ -299,7 +316,6 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
             if (hits_local) atomicAdd(&n_hits, hits_local);
             if (valid_local) atomicAdd(&n_valid, valid_local);
         }
-        __syncthreads();
 
         // ---- P5: new LRU order ----
         // thread t owns s_order[t*IPT_S, (t+1)*IPT_S); entries in [E, resident0) are the
@@ -388,7 +404,7 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
             }
         }
         if (bits) flag_status(status, r, bits);
-        __syncthreads();
+        if (r + gridDim.x < req_num) __syncthreads();  // shared memory is reused by the next request
     }
 }
 
@@ -402,10 +418,10 @@ inline uint32_t pow2ceil(uint32_t x) {
 inline size_t lru_smem_bytes(uint32_t S, uint32_t Q, int* log2h_out) {
     const uint64_t Sp = (S + 3) & ~3u;
     uint32_t h = 2 * pow2ceil(Q < 16 ? 16 : Q);
-    size_t bytes = (2ull * Sp + 3ull * h) * sizeof(int32_t);
+    size_t bytes = (2ull * Sp + 4ull * h) * sizeof(int32_t);
     if (bytes > 200u * 1024u) {  // large S and Q together: load factor up to 1 (still terminates)
         h /= 2;
-        bytes = (2ull * Sp + 3ull * h) * sizeof(int32_t);
+        bytes = (2ull * Sp + 4ull * h) * sizeof(int32_t);
     }
     int l = 0;
     while ((1u << l) < h) ++l;

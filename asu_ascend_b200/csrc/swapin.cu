@@ -23,6 +23,7 @@ namespace {
 constexpr int kWarps = 8;
 constexpr int kUnroll = 8;
 
+template <bool kPeer>
 __global__ void __launch_bounds__(kWarps * 32)
 swapin_kernel(const int4* host, int64_t pool_rows, uint32_t cpr, uint32_t pitch16,
               const int32_t* __restrict__ rec, uint32_t K, const int32_t* __restrict__ query,
@@ -98,6 +99,9 @@ swapin_kernel(const int4* host, int64_t pool_rows, uint32_t cpr, uint32_t pitch1
         }
         __syncwarp();
     }
+    // rows stored into another GPU's memory: performed at system scope before the grid
+    // completes, so whatever the host orders after this launch sees them
+    if constexpr (kPeer) __threadfence_system();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -134,6 +138,10 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
+// kPeer: the slot pool is another GPU's memory (a CUDA IPC mapping reached over NVLink).  The row
+// is then written from shared memory with plain 16-byte stores instead of a bulk store, and every
+// thread fences at system scope before it exits.
+template <bool kPeer>
 __global__ void __launch_bounds__(kBulkWarps * 32)
 swapin_bulk_kernel(const uint8_t* host, int64_t pool_rows, uint32_t row_bytes, uint32_t pitch,
                    const int32_t* __restrict__ rec, uint32_t K, const int32_t* __restrict__ query,
@@ -175,7 +183,8 @@ swapin_bulk_kernel(const uint8_t* host, int64_t pool_rows, uint32_t row_bytes, u
         }
         const uint8_t* src = host + static_cast<uint64_t>(row) * pitch;
         uint8_t* dst = pool + (static_cast<uint64_t>(r) * S + s) * row_bytes;
-        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the slot's last store has read it
+        if constexpr (!kPeer)
+            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the slot's last store has read it
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(my_bar), "r"(row_bytes)
                      : "memory");
         asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -188,12 +197,23 @@ swapin_bulk_kernel(const uint8_t* host, int64_t pool_rows, uint32_t row_bytes, u
             break;
         }
         parity ^= 1u;
-        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(my_slot),
-                     "r"(row_bytes)
-                     : "memory");
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        if constexpr (kPeer) {
+            // the bulk copy completed on the mbarrier: its bytes are visible to this thread
+            const int4* s16 = reinterpret_cast<const int4*>(slots + (w * 32 + lane) * slot_stride);
+            int4* d16 = reinterpret_cast<int4*>(dst);
+            for (uint32_t c = 0; c < row_bytes / 16; ++c) d16[c] = s16[c];
+        } else {
+            asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(my_slot),
+                         "r"(row_bytes)
+                         : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
     }
-    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // every store done before the CTA exits
+    if constexpr (kPeer) {
+        __threadfence_system();  // peer stores performed before the grid completes
+    } else {
+        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // every store done before the CTA exits
+    }
 }
 
 // Self-test of the swap-in's bounded wait (mbar_wait): one thread waits on an mbarrier with an
@@ -217,21 +237,20 @@ using namespace asu;
 
 namespace {
 
-// Dynamic shared memory limit of swapin_bulk_kernel, configured once per device.
+// Dynamic shared memory limit of swapin_bulk_kernel<kPeer>, configured once per device.
+template <bool kPeer>
 int bulk_configure(uint32_t smem) {
     int max_dynamic = 0;
-    const int rc = asu_max_dynamic_smem(reinterpret_cast<const void*>(swapin_bulk_kernel), &max_dynamic);
+    const int rc = asu_max_dynamic_smem(reinterpret_cast<const void*>(swapin_bulk_kernel<kPeer>), &max_dynamic);
     if (rc != ASU_OK) return rc;
     return smem <= static_cast<uint32_t>(max_dynamic) ? ASU_OK : ASU_ERR_ARG;
 }
 
-}  // namespace
-
-extern "C" int asu_swapin_gather(void* stream, const void* host_pool, int64_t pool_rows, uint32_t row_bytes,
-                                 uint32_t host_pitch, const int32_t* record_addr, uint32_t key_space,
-                                 const int32_t* query, const int32_t* slot, const uint8_t* install_mask,
-                                 uint32_t query_count,
-                                 void* slot_pool, uint32_t slot_count, uint32_t req_num, int32_t* status) {
+template <bool kPeer>
+int swapin_launch(void* stream, const void* host_pool, int64_t pool_rows, uint32_t row_bytes, uint32_t host_pitch,
+                  const int32_t* record_addr, uint32_t key_space, const int32_t* query, const int32_t* slot,
+                  const uint8_t* install_mask, uint32_t query_count, void* slot_pool, uint32_t slot_count,
+                  uint32_t req_num, int32_t* status) {
     if (req_num == 0 || query_count == 0) return ASU_OK;
     if (!host_pool || !record_addr || !query || !slot || !install_mask || !slot_pool || pool_rows <= 0 ||
         row_bytes == 0 || key_space == 0 || slot_count == 0)
@@ -245,13 +264,13 @@ extern "C" int asu_swapin_gather(void* stream, const void* host_pool, int64_t po
     if (row_bytes <= kBulkMaxRow) {
         const uint32_t stride = (row_bytes + 127) / 128 * 128;
         const uint32_t smem = kBulkWarps * 32 * stride;
-        const int rc = bulk_configure(smem);
+        const int rc = bulk_configure<kPeer>(smem);
         if (rc != ASU_OK) return rc;
         uint64_t grid = (groups + kBulkWarps - 1) / kBulkWarps;
         const uint64_t per_sm = stride <= 768 ? 2 : 1;  // two CTAs per SM while their slots fit
         const uint64_t cap = static_cast<uint64_t>(asu_sm_count()) * per_sm;
         if (grid > cap) grid = cap;
-        return launch_pdl(swapin_bulk_kernel, dim3(static_cast<uint32_t>(grid)), dim3(kBulkWarps * 32), smem,
+        return launch_pdl(swapin_bulk_kernel<kPeer>, dim3(static_cast<uint32_t>(grid)), dim3(kBulkWarps * 32), smem,
                           static_cast<cudaStream_t>(stream), static_cast<const uint8_t*>(host_pool), pool_rows,
                           row_bytes, host_pitch, record_addr, key_space, query, slot, install_mask, query_count,
                           static_cast<uint8_t*>(slot_pool), slot_count, req_num, status, stride);
@@ -259,10 +278,30 @@ extern "C" int asu_swapin_gather(void* stream, const void* host_pool, int64_t po
     uint64_t grid = (groups + kWarps - 1) / kWarps;
     const uint64_t cap = static_cast<uint64_t>(asu_sm_count()) * 8ull;
     if (grid > cap) grid = cap;
-    return launch_pdl(swapin_kernel, dim3(static_cast<uint32_t>(grid)), dim3(kWarps * 32), 0,
+    return launch_pdl(swapin_kernel<kPeer>, dim3(static_cast<uint32_t>(grid)), dim3(kWarps * 32), 0,
                       static_cast<cudaStream_t>(stream), static_cast<const int4*>(host_pool), pool_rows,
                       row_bytes / 16, host_pitch / 16, record_addr, key_space, query, slot, install_mask, query_count,
                       static_cast<int4*>(slot_pool), slot_count, req_num, status);
+}
+
+}  // namespace
+
+extern "C" int asu_swapin_gather(void* stream, const void* host_pool, int64_t pool_rows, uint32_t row_bytes,
+                                 uint32_t host_pitch, const int32_t* record_addr, uint32_t key_space,
+                                 const int32_t* query, const int32_t* slot, const uint8_t* install_mask,
+                                 uint32_t query_count,
+                                 void* slot_pool, uint32_t slot_count, uint32_t req_num, int32_t* status) {
+    return swapin_launch<false>(stream, host_pool, pool_rows, row_bytes, host_pitch, record_addr, key_space, query,
+                                slot, install_mask, query_count, slot_pool, slot_count, req_num, status);
+}
+
+extern "C" int asu_swapin_gather_to_peer(void* stream, const void* host_pool, int64_t pool_rows, uint32_t row_bytes,
+                                         uint32_t host_pitch, const int32_t* record_addr, uint32_t key_space,
+                                         const int32_t* query, const int32_t* slot, const uint8_t* install_mask,
+                                         uint32_t query_count, void* peer_slot_pool, uint32_t slot_count,
+                                         uint32_t req_num, int32_t* status) {
+    return swapin_launch<true>(stream, host_pool, pool_rows, row_bytes, host_pitch, record_addr, key_space, query,
+                               slot, install_mask, query_count, peer_slot_pool, slot_count, req_num, status);
 }
 
 extern "C" int asu_host_pool_alloc(uint64_t bytes, void** host_ptr, void** device_ptr) {

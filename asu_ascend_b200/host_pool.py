@@ -11,11 +11,45 @@ position into ``slot_pool[r, slot]`` with one kernel that reads host memory dire
 from __future__ import annotations
 
 import ctypes
+import mmap
+import os
 
 import numpy as np
 import torch
 
 from ._lib import check, lib, raise_on_status
+
+
+class SharedRows:
+    """Rows in an anonymous shared-memory file (memfd): the backing of a host pool that other
+    processes of the box map too.  ``fd`` can be handed to another process (over a Unix socket,
+    see ``balance.py``), which maps the same pages with ``SharedRows(nbytes, fd=received_fd)``.
+    No CUDA here: page-locking and GPU mapping are the pool's job."""
+
+    def __init__(self, nbytes: int, fd: int | None = None):
+        if nbytes <= 0:
+            raise ValueError("nbytes must be positive")
+        if fd is None:
+            fd = os.memfd_create("asu-host-pool", os.MFD_CLOEXEC)
+            os.ftruncate(fd, nbytes)
+        elif os.fstat(fd).st_size < nbytes:
+            os.close(fd)
+            raise ValueError("the shared file is smaller than the pool")
+        self.fd, self.nbytes = fd, nbytes
+        self.mm = mmap.mmap(fd, nbytes, mmap.MAP_SHARED, mmap.PROT_READ | mmap.PROT_WRITE)
+        self.flat = np.frombuffer(self.mm, dtype=np.uint8)
+        self.address = self.flat.ctypes.data
+
+    def close(self) -> None:
+        if self.mm is None:
+            return
+        self.flat = None
+        try:
+            self.mm.close()
+        except BufferError:  # a view is still referenced elsewhere: the pages go at process exit
+            pass
+        os.close(self.fd)
+        self.mm = None
 
 
 class HostRowPool:
@@ -26,9 +60,14 @@ class HostRowPool:
     one TMA bulk copy each, and a row that starts on a 128-byte boundary is read from host
     memory in whole 128-byte lines (measured on B200 with 656-byte rows: ~48 GB/s at a 768-byte
     pitch, ~41 GB/s packed).  ``array`` is a [rows, row_bytes] view of the records.
+
+    ``shared=True`` backs the pool with a shared-memory file (``SharedRows``) registered for this
+    process's GPU, so another rank of the box can map the same rows (``HostRowPool.attach``) and
+    swap them in through its own host link.  The default is a plain cudaHostAlloc allocation.
     """
 
-    def __init__(self, rows: int, row_bytes: int, pitch: int | None = None):
+    def __init__(self, rows: int, row_bytes: int, pitch: int | None = None, shared: bool = False,
+                 _fd: int | None = None):
         if rows <= 0 or row_bytes <= 0 or row_bytes % 16:
             raise ValueError("rows must be positive and row_bytes a positive multiple of 16")
         if pitch is None:
@@ -37,14 +76,30 @@ class HostRowPool:
             raise ValueError("pitch must be a multiple of 16 and at least row_bytes")
         self.rows, self.row_bytes, self.pitch = rows, row_bytes, pitch
         self.nbytes = rows * pitch
+        self.shared = None
         host = ctypes.c_void_p()
         dev = ctypes.c_void_p()
-        check(lib.asu_host_pool_alloc(self.nbytes, ctypes.byref(host), ctypes.byref(dev)), "asu_host_pool_alloc")
-        self._host = host.value
+        if shared or _fd is not None:
+            self.shared = SharedRows(self.nbytes, _fd)
+            rc = lib.asu_host_register(self.shared.address, self.nbytes, ctypes.byref(dev))
+            if rc != 0:
+                self.shared.close()
+                check(rc, "asu_host_register")
+            self._host = self.shared.address
+            buf = self.shared.flat
+        else:
+            check(lib.asu_host_pool_alloc(self.nbytes, ctypes.byref(host), ctypes.byref(dev)), "asu_host_pool_alloc")
+            self._host = host.value
+            buf = np.frombuffer((ctypes.c_uint8 * self.nbytes).from_address(self._host), dtype=np.uint8)
         self.device_ptr = dev.value
-        buf = (ctypes.c_uint8 * self.nbytes).from_address(self._host)
-        self.array = np.frombuffer(buf, dtype=np.uint8).reshape(rows, pitch)[:, :row_bytes]
+        self.array = buf.reshape(rows, pitch)[:, :row_bytes]
         self.tensor = torch.from_numpy(self.array)  # CPU view of the same pinned bytes
+
+    @classmethod
+    def attach(cls, fd: int, rows: int, row_bytes: int, pitch: int) -> "HostRowPool":
+        """Map another process's shared pool (its ``shared.fd``, received by this process) and
+        register it for this process's GPU.  The pool takes ownership of ``fd``."""
+        return cls(rows, row_bytes, pitch, _fd=fd)
 
     def fill_random(self, seed: int) -> None:
         rng = np.random.Generator(np.random.PCG64(seed))
@@ -57,7 +112,11 @@ class HostRowPool:
         if getattr(self, "_host", None):
             self.array = None
             self.tensor = None
-            check(lib.asu_host_pool_free(self._host), "asu_host_pool_free")
+            if self.shared is not None:
+                check(lib.asu_host_unregister(self._host), "asu_host_unregister")
+                self.shared.close()
+            else:
+                check(lib.asu_host_pool_free(self._host), "asu_host_pool_free")
             self._host = None
 
     def __del__(self):
@@ -91,6 +150,32 @@ class HostRowPool:
                 query.data_ptr(), slot.data_ptr(), install.data_ptr(), Q, slot_pool.data_ptr(), slot_pool.shape[1],
                 R, None if status is None else status.data_ptr()), "asu_swapin_gather")
 
+
+    def swapin_to_peer(self, record_addr: torch.Tensor, query: torch.Tensor, slot: torch.Tensor,
+                       install: torch.Tensor, peer_slot_pool: int, slot_count: int,
+                       status: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> None:
+        """``swapin`` into another GPU's slot pool: ``peer_slot_pool`` is the device address (in this
+        process) of a CUDA IPC mapping of a [R, slot_count, row_bytes] pool on a peer GPU.  The
+        index tensors live on this process's GPU.  The rows land in the peer's memory before the
+        launch completes (system-scope fence), so work ordered after it on ``stream`` may signal
+        the peer."""
+        dev = query.device
+        R, Q = query.shape
+        for name, t in (("record_addr", record_addr), ("query", query), ("slot", slot)):
+            if t.dtype != torch.int32 or t.device != dev or not t.is_contiguous():
+                raise RuntimeError(f"{name} must be a contiguous int32 CUDA tensor on {dev}")
+        if install.dtype not in (torch.bool, torch.uint8) or install.shape != query.shape or not install.is_contiguous():
+            raise RuntimeError("install must be a contiguous bool/uint8 tensor shaped like query")
+        if record_addr.dim() != 2 or record_addr.shape[0] != R:
+            raise RuntimeError("record_addr must be [R, key_space]")
+        if not peer_slot_pool:
+            raise RuntimeError("peer_slot_pool must be a mapped peer address")
+        s = (stream or torch.cuda.current_stream(dev)).cuda_stream
+        with torch.cuda.device(dev):
+            check(lib.asu_swapin_gather_to_peer(
+                s, self.device_ptr, self.rows, self.row_bytes, self.pitch, record_addr.data_ptr(), record_addr.shape[1],
+                query.data_ptr(), slot.data_ptr(), install.data_ptr(), Q, peer_slot_pool, slot_count, R,
+                None if status is None else status.data_ptr()), "asu_swapin_gather_to_peer")
 
     def writeback(self, src: torch.Tensor, dst_rows: torch.Tensor, src_index: torch.Tensor | None = None,
                   status: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> None:

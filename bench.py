@@ -127,6 +127,17 @@ def parse_args():
     p.add_argument("--host-pitch", type=int, default=0,
                    help="bytes between host-pool rows (0: the pool's default, rows up to 1 KiB padded "
                         "to a multiple of 128 bytes)")
+    p.add_argument("--no-balance", action="store_true",
+                   help="resolver workloads on N > 1 GPUs: no swap-in balancing between ranks")
+    p.add_argument("--balance-share", type=int, default=0,
+                   help="N > 1: skip the calibration and let rank 1 swap in the last M requests of rank 0 "
+                        "(a fixed plan for checking the balanced path)")
+    p.add_argument("--shared-pool", action="store_true",
+                   help="1 GPU: back the host pool with a shared-memory file registered with the GPU "
+                        "(the pool every rank uses on N > 1 GPUs) instead of cudaHostAlloc")
+    p.add_argument("--verify", action="store_true",
+                   help="resolver workloads: after the run, check every resident slot row of every "
+                        "request against its host record (GPU-side compare)")
     return p.parse_args()
 
 
@@ -303,6 +314,7 @@ def resolver_config(args, cfg: ResolverCfg, req_per_gpu: int, world: int) -> dic
 # ------------------------------------------------------------------ CPU side
 
 CPU_CYCLE_STEPS = 32  # distinct top-k sets the CPU legs cycle through (fewer would repeat into hits)
+CAL_STEPS, CAL_ROUNDS = 3, 2  # swap-in balancing on N > 1 GPUs: steps per calibration round, refinements
 
 
 def cpu_port_run(cfg: ResolverCfg, req: int, trace: np.ndarray, prefill: int, timed: int, time_cap_s: float,
@@ -447,7 +459,9 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     else:
         r0, R = rank * cfg.req, cfg.req
     K_steps, W, L = args.steps, args.warmup, cfg.layers
-    base = args.prefill + W
+    balance = world > 1 and not args.no_balance
+    cal = 0 if not balance or args.balance_share else CAL_STEPS * (1 + CAL_ROUNDS)
+    base = args.prefill + cal + W
     cpu_leg = world == 1 and not args.no_cpu_baseline and cfg.name == "resolver"
     n_steps = base + (max(2 * K_steps, CPU_CYCLE_STEPS) if cpu_leg else 2 * K_steps)
     trace = make_trace(cfg, R, trace_seed(args, r0), n_steps)
@@ -459,7 +473,8 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     # the pinned pool goes on the NUMA node of this GPU's host CPUs (a no-op on single-node hosts)
     all_cpus = os.sched_getaffinity(0)
     bound_cpus = bind_to_gpu_local_cpus(gpu_index(local_rank))
-    host = HostRowPool(POOL_ROWS if cfg.row <= 4096 else POOL_ROWS // 64, cfg.row, pitch=args.host_pitch or None)
+    host = HostRowPool(POOL_ROWS if cfg.row <= 4096 else POOL_ROWS // 64, cfg.row, pitch=args.host_pitch or None,
+                       shared=balance or args.shared_pool)
     host.fill_random(11 + rank)
     recs = [record_addresses_torch(R, cfg.keys, host.rows, dev, key_offset=layer * cfg.keys,
                                    row_stride=cfg.keys * L) for layer in range(L)]
@@ -470,14 +485,44 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     flush = L2Flush(torch, dev)
     h2d_alone, h2d_peak = h2d_peaks(torch, dev, world, rank)
 
+    bal = None
+    if balance:
+        from asu_ascend_b200.balance import SwapinBalancer
+
+        bal = SwapinBalancer(host, recs, slot_pools, status, cfg.topk)
+
+    def swapin(layer, q, o):
+        if bal is not None:
+            bal.swapin(layer, q, o)
+        else:
+            host.swapin(recs[layer], q, o.slot, o.install, slot_pools[layer], status=status)
+
     def total_stats():
         return sum(p.stats.sum(0) for p in pools)
 
-    for i in range(base):  # untimed: fill the pools, then warm up
-        for layer in range(L):
-            o = outs[(i * L + layer) % 2]
-            pools[layer].step(q_dev[i, layer], out=o)
-            host.swapin(recs[layer], q_dev[i, layer], o.slot, o.install, slot_pools[layer], status=status)
+    def run_steps(first, n):
+        for i in range(first, first + n):
+            for layer in range(L):
+                o = outs[(i * L + layer) % 2]
+                pools[layer].step(q_dev[i, layer], out=o)
+                swapin(layer, q_dev[i, layer], o)
+
+    run_steps(0, args.prefill)  # untimed: fill the pools
+    balance_info = None
+    if bal is not None:
+        rank_sync(torch)
+        if args.balance_share:
+            bal.set_plan([(0, 1, args.balance_share)])
+            balance_info = {"pairs": [[0, 1, args.balance_share]], "fixed": True}
+        else:
+            done = [args.prefill]
+
+            def cal_steps(n):
+                run_steps(done[0], n)
+                done[0] += n
+
+            balance_info = bal.calibrate(cal_steps, steps=CAL_STEPS, rounds=CAL_ROUNDS)
+    run_steps(args.prefill + cal, W)  # untimed warm-up
     rank_sync(torch)
 
     # per step and layer: [a] resolve [b] swap-in [c]; the free-count snapshots sit outside
@@ -500,7 +545,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             a.record()
             pools[layer].step(q, out=o)
             b.record()
-            host.swapin(recs[layer], q, o.slot, o.install, slot_pools[layer], status=status)
+            swapin(layer, q, o)
             c.record()
             free_after[k * L + layer] = pools[layer].free_count.sum()
             evicting[k * L + layer] = (o.evicted_count > 0).sum()
@@ -538,7 +583,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             with torch.cuda.stream(copy_stream):
                 slot_host.copy_(o.slot, non_blocking=True)
                 hit_host.copy_(o.hit, non_blocking=True)
-            host.swapin(recs[layer], q_in, o.slot, o.install, slot_pools[layer], status=status)
+            swapin(layer, q_in, o)
             main.wait_stream(copy_stream)  # the outputs' buffer is reused two layers later
         ev2[k][1].record()
     rank_sync(torch)
@@ -546,6 +591,11 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     for p in pools:
         p.check_status()
     check_status(status, "swapin")
+    if bal is not None:
+        bal.check_status()
+    verified = None
+    if args.verify:
+        verified = verify_resident_rows(torch, host, recs, pools, slot_pools)
 
     max_ms, max_e2e_ms = max_over_ranks([sum(step_ms), sum(e2e_ms)], dev)  # slowest rank
     job_stats = reduce_stats(torch.stack([p.stats for p in pools])).cpu().tolist()  # end-of-run (NCCL)
@@ -614,11 +664,32 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             "job_stats": dict(zip(LruSlotPools.STAT_NAMES, job_stats)),
             "host_cpus_bound": len(bound_cpus),
             "note_step_time": "sum over layers of (resolve + swap-in) event intervals",
+            "balance": balance_info,
+            "verified_rows": verified,
             "cpu_baseline": cpu,
             "clocks": clk,
         })
         print(json.dumps(line), flush=True)
+    if bal is not None:
+        bal.close()
     host.close()
+
+
+def verify_resident_rows(torch, host, recs, pools, slot_pools) -> int:
+    """Every resident slot row of every request equals its host record (compared on the GPU);
+    returns the rows checked and raises on the first request with a mismatch."""
+    dev = slot_pools[0].device
+    host_dev = host.tensor.to(dev)  # [rows, row_bytes], the pool without its row padding
+    checked = 0
+    for layer, (p, sp) in enumerate(zip(pools, slot_pools)):
+        s2t = p.slot_to_token
+        for r in range(s2t.shape[0]):
+            slots = torch.nonzero(s2t[r] >= 0).flatten()
+            rows = recs[layer][r, s2t[r, slots].long()].long()
+            if not torch.equal(sp[r, slots], host_dev[rows]):
+                raise RuntimeError(f"layer {layer} request {r}: a resident slot row differs from its host record")
+            checked += slots.numel()
+    return checked
 
 
 # ------------------------------------------------------------------ single-request LRU (CPU reference config)
@@ -1342,7 +1413,7 @@ def main():
         import torch.distributed as dist
 
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     try:
         if args.workload in RESOLVER_WORKLOADS:
             run_resolver(args, RESOLVER_WORKLOADS[args.workload], world, rank, local_rank)

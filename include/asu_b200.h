@@ -222,6 +222,37 @@ int asu_host_device_pointer(const void* host_ptr, void** device_ptr);
  * `stream`; the kernel returns either way and the context stays usable. */
 int asu_selftest_bounded_wait(void* stream, int32_t arrive, int32_t* status);
 
+/* ---- swap-in balancing across the GPUs of one box -------------------------
+ * No reference counterpart: the reference's swap-in is a per-request MicroKV socket fetch on one
+ * NPU (docs/v0.1/kv-cache-offload-v0.1-real-ops-design.md:293-312).  On a box whose GPUs share
+ * the host memory system unevenly, a rank on a fast host link swaps in part of a slow rank's rows:
+ * it reads them from the slow rank's host pool over its own link and stores them into the slow
+ * rank's slot pool over NVLink. */
+
+/* asu_swapin_gather with a slot pool in ANOTHER GPU's memory (peer_slot_pool: a CUDA IPC mapping
+ * opened with asu_ipc_open, device peer access over NVLink).  Same arguments and status bits; rows
+ * are written with plain 16-byte stores (no bulk or multicast copy touches the peer), and every
+ * thread fences at system scope before the grid completes, so work ordered after this launch (an
+ * event or a NCCL message the peer waits on) sees the rows. */
+int asu_swapin_gather_to_peer(void* stream, const void* host_pool, int64_t pool_rows, uint32_t row_bytes,
+                              uint32_t host_pitch, const int32_t* record_addr, uint32_t key_space,
+                              const int32_t* query, const int32_t* slot, const uint8_t* install_mask,
+                              uint32_t query_count, void* peer_slot_pool, uint32_t slot_count, uint32_t req_num,
+                              int32_t* status);
+
+/* Page-lock and map existing host memory (e.g. another process's pool mapped from a shared-memory
+ * file descriptor) for this process's CUDA context: cudaHostRegister(Portable|Mapped). */
+int asu_host_register(void* host_ptr, uint64_t bytes, void** device_ptr);
+int asu_host_unregister(void* host_ptr);
+
+/* CUDA IPC of a device allocation: `handle` (64 bytes) names the allocation that contains
+ * device_ptr, `offset` is device_ptr's distance from its start.  asu_ipc_open maps it into the
+ * calling process on the current device (peer access enabled lazily) and returns the mapping's
+ * base; asu_ipc_close unmaps it. */
+int asu_ipc_export(const void* device_ptr, uint8_t* handle, uint64_t* offset);
+int asu_ipc_open(const uint8_t* handle, void** base_ptr);
+int asu_ipc_close(void* base_ptr);
+
 /* ======================================================================
  * single-request KV resolver (patch 0001 asu_kv_resolver custom op)
  * ==================================================================== */

@@ -1,0 +1,168 @@
+"""Swap-in balancing between ranks, host side on CPU: the plan (pairs and shares), the hand-over of
+the owner's shared host pool to the helper, and the split of one step's installs between the two
+ranks as world-size-2 gloo ranks: the owner's slot pool after its own part plus the helper's part
+equals the oracle's swap-in of every request, byte for byte.  The GPU path (peer stores over
+NVLink, NCCL messages) runs the same split through ``bench.py --balance-share`` on two GPUs."""
+
+import os
+import socket
+import threading
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from asu_ascend_b200.balance import (FdServer, balanced_share, fetch_fd, plan_pairs, refine_share,
+                                     socket_name)
+from asu_ascend_b200.host_pool import SharedRows
+
+
+def test_balanced_share_equalises_finish_times():
+    rng = np.random.default_rng(3)
+    for _ in range(200):
+        ro, rh = int(rng.integers(2, 300)), int(rng.integers(1, 300))
+        bo, bh = float(rng.uniform(1, 60)), float(rng.uniform(1, 60))
+        m = balanced_share(ro, rh, bo, bh)
+        assert 0 <= m <= ro - 1
+        cost = lambda k: max((ro - k) / bo, (rh + k) / bh)  # noqa: E731
+        best = min(range(ro), key=cost)
+        assert cost(m) <= cost(best) + max(1 / bo, 1 / bh) + 1e-12  # within one request of the optimum
+    assert balanced_share(128, 128, 30.0, 30.0) == 0
+    assert balanced_share(128, 128, 0.0, 30.0) == 0
+    assert balanced_share(1, 128, 1.0, 100.0) == 0
+
+
+def test_plan_pairs_slowest_with_fastest():
+    # the 8-GPU box's H2D rates with all ranks copying: GPU 0-3 ~22 GB/s, GPU 4-7 ~35.6 GB/s
+    rates = [22.0, 22.5, 21.8, 22.2, 35.6, 35.0, 36.0, 35.4]
+    pairs = plan_pairs(rates, [128] * 8)
+    assert sorted(o for o, _, _ in pairs) == [0, 1, 2, 3]
+    assert sorted(h for _, h, _ in pairs) == [4, 5, 6, 7]
+    assert (2, 6, balanced_share(128, 128, 21.8, 36.0)) in pairs  # slowest with fastest
+    for o, h, m in pairs:
+        assert 25 <= m <= 35
+    assert plan_pairs([30.0] * 8, [128] * 8) == []                  # nothing to balance
+    assert plan_pairs([30.0, 30.2], [128, 128]) == []                # below the minimum share
+    assert plan_pairs([10.0, 30.0, 20.0], [64, 64, 64]) == [(0, 1, 32)]  # odd count: the middle rank stays alone
+    with pytest.raises(ValueError):
+        plan_pairs([1.0, 2.0], [1])
+
+
+def test_refine_share_moves_towards_the_slower_side():
+    # with m = 20 the owner still took longer: the helper takes more
+    assert refine_share(128, 128, 20, owner_ms=1.2, helper_ms=1.0) > 20
+    assert refine_share(128, 128, 40, owner_ms=0.8, helper_ms=1.2) < 40
+    assert refine_share(128, 128, 30, owner_ms=0.0, helper_ms=1.0) == 30
+
+
+def test_fd_hand_over_shares_the_pool_pages():
+    rows = SharedRows(1 << 16)
+    rows.flat[:] = np.arange(1 << 16, dtype=np.uint32).astype(np.uint8)
+    name = socket_name(os.urandom(4).hex(), 0)
+    server = FdServer(name)
+    t = threading.Thread(target=server.serve, args=(rows.fd, b'{"rows": 7}'))
+    t.start()
+    fd, payload = fetch_fd(name, timeout_s=10)
+    t.join()
+    server.close()
+    assert payload == b'{"rows": 7}'
+    other = SharedRows(1 << 16, fd=fd)
+    try:
+        assert np.array_equal(other.flat, rows.flat)
+        other.flat[100] = 201  # the same pages: a write through one mapping shows in the other
+        assert rows.flat[100] == 201
+    finally:
+        other.close()
+        rows.close()
+    with pytest.raises(TimeoutError):
+        fetch_fd(socket_name(os.urandom(4).hex(), 1), timeout_s=0.2)
+
+
+# ---- one step split between an owner and a helper (gloo) ----
+
+R, K, S, Q, ROW, PITCH, ROWS, M = 6, 4096, 512, 128, 64, 128, 2048, 2
+
+
+def _owner_steps():
+    """Three LRU steps of R requests (oracle) with their swap-in inputs."""
+    from asu_ascend_b200.workloads import LocalityTrace, record_addresses
+    from oracle import asu_oracle as O
+
+    tr = LocalityTrace(R, K, topk=Q, seed=21)
+    pools = [O.LruPool(S, 64) for _ in range(R)]
+    out = []
+    for _ in range(3):
+        q = tr.step()
+        res = [pools[r].step(q[r]) for r in range(R)]
+        out.append((q, np.stack([x.slot for x in res]).astype(np.int32),
+                    np.stack([x.install for x in res]).astype(np.uint8)))
+    return out, record_addresses(R, K, ROWS)
+
+
+def _worker(rank, port, token, out_path):
+    from oracle import asu_oracle as O
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    try:
+        steps, rec = _owner_steps()
+        if rank == 0:  # owner: slow link, keeps requests [0, R - M)
+            pool = SharedRows(ROWS * PITCH)
+            host = pool.flat.reshape(ROWS, PITCH)[:, :ROW]
+            host[:] = np.random.default_rng(5).integers(0, 256, host.shape, dtype=np.uint8)
+            server = FdServer(socket_name(token, 0))
+            dist.barrier()
+            server.serve(pool.fd, b"{}")
+            server.close()
+            dist.send(torch.from_numpy(rec), 1)  # the record tables, once
+            slot_pool = np.zeros((R, S, ROW), np.uint8)
+            k = R - M
+            for q, slot, inst in steps:
+                for t in (q, slot, inst):
+                    dist.send(torch.from_numpy(np.ascontiguousarray(t[k:])), 1)
+                slot_pool[:k] = O.swapin(host, rec[:k], q[:k], slot[:k], inst[:k], slot_pool[:k])
+                # the helper's rows: on the GPU it stores them into this pool over NVLink
+                rows = torch.empty((M, Q, ROW), dtype=torch.uint8)
+                dist.recv(rows, 1)
+                rr, pp = np.nonzero(inst[k:])
+                slot_pool[k + rr, slot[k + rr, pp]] = rows.numpy()[rr, pp]
+            expect = np.zeros_like(slot_pool)
+            for q, slot, inst in steps:
+                expect = O.swapin(host, rec, q, slot, inst, expect)
+            np.save(out_path, np.array([np.array_equal(slot_pool, expect), int(expect.any(axis=2).sum())]))
+            pool.close()
+        else:  # helper: maps the owner's pool and swaps in its last M requests
+            dist.barrier()
+            fd, _ = fetch_fd(socket_name(token, 0), timeout_s=30)
+            owner_pool = SharedRows(ROWS * PITCH, fd=fd)
+            host = owner_pool.flat.reshape(ROWS, PITCH)[:, :ROW]
+            rec_copy = torch.empty((R, K), dtype=torch.int32)
+            dist.recv(rec_copy, 0)
+            for _ in steps:
+                q = torch.empty((M, Q), dtype=torch.int32)
+                slot = torch.empty((M, Q), dtype=torch.int32)
+                inst = torch.empty((M, Q), dtype=torch.uint8)
+                for t in (q, slot, inst):
+                    dist.recv(t, 0)
+                q, inst = q.numpy(), inst.numpy()
+                rows = np.zeros((M, Q, ROW), np.uint8)
+                rr, pp = np.nonzero(inst)
+                rows[rr, pp] = host[rec_copy.numpy()[R - M + rr, q[rr, pp]]]
+                dist.send(torch.from_numpy(rows), 0)
+            owner_pool.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_owner_and_helper_split_one_step_byte_exact(tmp_path):
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    out = tmp_path / "ok.npy"
+    mp.spawn(_worker, args=(port, os.urandom(4).hex(), str(out)), nprocs=2, join=True)
+    ok, resident = np.load(out)
+    assert ok == 1
+    assert resident > 0
