@@ -283,23 +283,30 @@ class SwapinBalancer:
         total = statistics.median(a.elapsed_time(c) for a, _, c in ev)
         return own, total
 
-    def calibrate(self, run_steps: Callable[[int], None], steps: int = 3, rounds: int = 2) -> dict:
+    def calibrate(self, run_steps: Callable[[int], None], steps: int = 3, rounds: int = 2,
+                  initial_pairs: list[tuple[int, int, int]] | None = None) -> dict:
         """Choose the pairs and shares.  ``run_steps(n)`` runs n steps of the caller's loop (which
-        swaps in through ``self.swapin``); every rank must call this with the same arguments."""
-        own, total = self._measure(run_steps, steps)
-        g = self._gather([float(self.R), total])
-        req = [int(x) for x in g[:, 0].tolist()]
-        rates = [req[r] / g[r, 1].item() if g[r, 1] > 0 else 0.0 for r in range(self.world)]
-        self.history.append({"round": 0, "ms": g[:, 1].tolist()})
-        self.set_plan(plan_pairs(rates, req, self.min_share))
+        swaps in through ``self.swapin``); every rank must call this with the same arguments.
+        ``initial_pairs`` skips the first round (the unbalanced measurement) and starts the
+        refinement from that plan."""
+        req = [int(x) for x in self._gather([float(self.R)])[:, 0].tolist()]
+        if initial_pairs is None:
+            own, total = self._measure(run_steps, steps)
+            g = self._gather([total])
+            rates = [req[r] / g[r, 0].item() if g[r, 0] > 0 else 0.0 for r in range(self.world)]
+            self.history.append({"round": 0, "ms": g[:, 0].tolist()})
+            self.set_plan(plan_pairs(rates, req, self.min_share))
+        else:
+            self.set_plan(initial_pairs)
         for i in range(rounds):
-            if not self.pairs:
+            if not any(m > 0 for _, _, m in self.pairs):
                 break
             own, total = self._measure(run_steps, steps)
             g = self._gather([own, total])
             self.history.append({"round": i + 1, "own_ms": g[:, 0].tolist(), "ms": g[:, 1].tolist(),
                                  "pairs": [list(p) for p in self.pairs]})
-            self.pairs = [(o, h, max(1, refine_share(req[o], req[h], m, g[o, 0].item(), g[h, 1].item())))
+            # a share refined to 0 leaves the pair in place but swaps in locally (no messages)
+            self.pairs = [(o, h, refine_share(req[o], req[h], m, g[o, 0].item(), g[h, 1].item()))
                           for o, h, m in self.pairs]
             self._apply_share()
         return {"pairs": [list(p) for p in self.pairs], "history": self.history}

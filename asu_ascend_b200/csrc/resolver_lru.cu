@@ -19,26 +19,40 @@
 // state array, lru_order [slots]: the first slots - free_slot_count entries are the resident
 // slots, least recently used first.
 //
-// B200 design: one launch, one CTA of 1024 threads (the request), the same phase structure as
-// the exact-LRU kernel (lru.cu):
-//  * all independent loads issued at launch: the free count, the order row (16-byte loads into
-//    shared memory), and per top-k entry its token's state, slot, record address and block;
-//  * the victims are the head of the order row; they are marked in shared memory, so an entry
-//    whose slot is a victim is classified as a miss with the state its token is restored to;
-//  * missing tokens claim their first position in a shared-memory hash, a block scan ranks the
-//    first occurrences in top-k order and rank k takes the k-th stack pop (the victims just
-//    pushed, top first, then the older entries), later duplicates read the slot from the hash;
-//  * every touch records its position per slot; the new order is [untouched residents in old
-//    order] ++ [touched slots by last touching position] (the OrderedDict order after the
-//    serial loop), built with block scans in shared memory;
-//  * the installs are listed in shared memory in rank order and the CTA copies their row pairs
-//    (16-, 4- or 1-byte units, several loads in flight per thread) after the state is written.
+// B200 design: one launch of one 8-CTA thread-block cluster (8 SMs) for the request.  The state
+// logic is one serial chain per call -- classify, rank, pop, reorder -- and runs in the leader
+// CTA (rank 0) with the exact-LRU kernel's phase structure (lru.cu); the parts bound by how many
+// random loads and row copies one SM keeps in flight are spread over the cluster:
+//  * gathers: each CTA loads its eighth of the top-k entries and their token state, slot,
+//    record address and block-table entry, and stores (token, state, slot, source row) into the
+//    leader's shared memory through distributed shared memory (DSMEM);
+//  * eviction: the victims are the head of the order row, lru_order[0, E); each CTA takes its
+//    share, marks them in the leader's last_pos table (-2: an entry whose slot is a victim is
+//    classified as a miss), and restores their tokens (ASU_ONLY with a record address, else
+//    TAIL_HBM), clears the slot's owner and pushes the slot on the free stack;
+//  * the leader meanwhile loads the order row into shared memory and gives the surviving
+//    residents last_pos = -1; a free slot gets its last touch when it is popped;
+//  * after a cluster barrier the leader classifies, de-duplicates misses in a shared-memory hash
+//    (first and last position per token), ranks first occurrences with a block scan (rank k takes
+//    the k-th stack pop: the victims just pushed, top first, then older entries), lists the
+//    installs in shared memory and arrives at a second cluster barrier; it then writes the
+//    outputs and the new order ([untouched residents in old order] ++ [touched slots by last
+//    touching position], the OrderedDict order after the serial loop);
+//  * the other seven CTAs wait at that barrier, copy the install list out of the leader's
+//    shared memory and copy the installed kv0 / kv1 row pairs (16-, 4- or 1-byte units, several
+//    loads in flight per thread) while the leader reorders.  A last cluster barrier keeps the
+//    leader's shared memory alive until every CTA has read the list.
+#include <cooperative_groups.h>
+
 #include "asu_common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace asu {
 namespace {
 
 constexpr int kThreads = 1024;
+constexpr int kCluster = 8;  // CTAs of the cluster; rank 0 is the leader
 constexpr int32_t kVictim = -2;  // last_pos marker of a slot evicted in this call
 constexpr int32_t kEmptyKey = -1;
 constexpr int kCopyUnroll = 8;
@@ -57,20 +71,20 @@ template <typename V>
 __device__ __forceinline__ void copy_rows(const int32_t* s_src, const int32_t* s_slot, int n,
                                           const uint8_t* __restrict__ kv0_src, const uint8_t* __restrict__ kv1_src,
                                           uint8_t* __restrict__ kv0_dst, uint8_t* __restrict__ kv1_dst, uint32_t c0,
-                                          uint32_t c1) {
+                                          uint32_t c1, uint32_t first_thread, uint32_t threads) {
     const V* s0 = reinterpret_cast<const V*>(kv0_src);
     const V* s1 = reinterpret_cast<const V*>(kv1_src);
     V* d0 = reinterpret_cast<V*>(kv0_dst);
     V* d1 = reinterpret_cast<V*>(kv1_dst);
     const uint64_t cpr = static_cast<uint64_t>(c0) + c1;
     const uint64_t total = static_cast<uint64_t>(n) * cpr;
-    for (uint64_t base = threadIdx.x; base < total; base += static_cast<uint64_t>(kThreads) * kCopyUnroll) {
+    for (uint64_t base = first_thread; base < total; base += static_cast<uint64_t>(threads) * kCopyUnroll) {
         V buf[kCopyUnroll];
         V* dst[kCopyUnroll];
 #pragma unroll
         for (int k = 0; k < kCopyUnroll; ++k) {
             dst[k] = nullptr;
-            const uint64_t u = base + static_cast<uint64_t>(k) * kThreads;
+            const uint64_t u = base + static_cast<uint64_t>(k) * threads;
             if (u >= total) continue;
             const uint64_t e = u / cpr;
             const uint64_t ch = u - e * cpr;
@@ -123,83 +137,55 @@ struct LruResolveArgs {
     int log2h;
 };
 
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// A gathered entry's token state and slot, packed for the leader: the state's category in bits
+// 16-17 (ASU_ONLY 0, HBM_RESIDENT 1, TAIL_HBM 2, anything else 3) and the slot in bits 0-15
+// (0xffff when it is not a slot of the pool).
+constexpr int32_t kCodeBadSlot = 0xffff;
+constexpr int32_t kCatBad = 3;
+
 template <int IPT_Q, int IPT_S>
-__global__ void __launch_bounds__(kThreads) resolve_lru_kernel(const LruResolveArgs a) {
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads) resolve_lru_kernel(const LruResolveArgs a) {
     pdl_wait();     // launched with launch_pdl: stream order for every access below
     pdl_trigger();  // the next launch on the stream may be scheduled now; it waits for this grid
     extern __shared__ __align__(16) int32_t smem[];
+    cg::cluster_group cluster = cg::this_cluster();
+    const unsigned crank = cluster.block_rank();
+    const bool leader = crank == 0;
     const uint32_t S = a.S, Q = a.Q;
     const uint32_t H = 1u << a.log2h;
     const uint32_t Sp = (S + 3) & ~3u;
     const uint32_t Qp = (Q + 3) & ~3u;
+    // the leader's layout (every CTA allocates it; the others use the front for the install list)
     int32_t* s_order = smem;         // [Sp] old order row, later the new one
-    int32_t* s_last = s_order + Sp;  // [Sp] last touching position, -1 untouched, -2 victim
-    int32_t* s_hkey = s_last + Sp;   // [H]  hash: token
-    int32_t* s_hpos = s_hkey + H;    // [H]  hash: first position
-    int32_t* s_hval = s_hpos + H;    // [H]  hash: installed slot
-    int32_t* s_isrc = s_hval + H;    // [Qp] installs in rank order: source row
-    int32_t* s_islot = s_isrc + Qp;  // [Qp] ... and managed slot
+    int32_t* s_last = s_order + Sp;  // [Sp] last touching position: -1 untouched, -2 victim
+    int32_t* s_hkey = s_last + Sp;   // [H]  hash: token (until the claims are done) ...
+    int32_t* s_hval = s_hkey;        //      ... then the installed slot
+    int32_t* s_hpos = s_hkey + H;    // [H]  hash: first position of the token
+    int32_t* s_hmax = s_hpos + H;    // [H]  hash: last position of the token
+    int32_t* g_code = s_hmax + H;    // [Qp] gathered per top-k entry: packed state and slot ...
+    int32_t* g_src = g_code + Qp;    // [Qp] ... and the source row should it miss
+    int32_t* s_isrc = g_code;        // [Qp] after the classification: installs in rank order, source row
+    int32_t* s_islot = g_src;        // [Qp] ... and managed slot
     __shared__ int scan_a[32], scan_b[32];
-    __shared__ int n_hits, n_valid;
+    __shared__ int n_hits, n_valid, s_ninst;
     const int tid = threadIdx.x;
     int32_t bits = 0;
 
-    // ---- P0: every independent load ----
+    // ---- P0 (every CTA): the free count, this CTA's share of the gathers and victims ----
+    // Distributed shared memory may be written once every CTA of the cluster has started: this
+    // barrier's arrival is here, its wait before the first remote store.
+    cluster_arrive();
     const int32_t free0 = ld_cg(a.count);
-    const bool vec_row = (S % 4 == 0) && (reinterpret_cast<uintptr_t>(a.order) % 16 == 0);
-    if (vec_row) {
-        constexpr int kVec = (IPT_S + 3) / 4;
-        const int4* src = reinterpret_cast<const int4*>(a.order);
-        int4* dst = reinterpret_cast<int4*>(s_order);
-        int4 ov[kVec];
-#pragma unroll
-        for (int j = 0; j < kVec; ++j)
-            if (tid + j * kThreads < S / 4) ov[j] = __ldcg(src + tid + j * kThreads);
-#pragma unroll
-        for (int j = 0; j < kVec; ++j)
-            if (tid + j * kThreads < S / 4) dst[tid + j * kThreads] = ov[j];
-    } else {
-        for (uint32_t i = tid; i < S; i += kThreads) s_order[i] = ld_cg(a.order + i);
-    }
-    int32_t tok[IPT_Q], st[IPT_Q], hs[IPT_Q], rec[IPT_Q], btv[IPT_Q];
-#pragma unroll
-    for (int j = 0; j < IPT_Q; ++j) {
-        const uint32_t pos = tid * IPT_Q + j;
-        tok[j] = -1;
-        st[j] = ASU_TOKEN_INVALID;
-        hs[j] = kNotFound;
-        rec[j] = -1;
-        btv[j] = -1;
-        if (pos < Q) {
-            const int32_t t = __ldg(a.topk + pos);
-            if (t >= 0 && t < a.limit) {
-                tok[j] = t;
-                st[j] = ld_cg(a.token_state + t);
-                hs[j] = ld_cg(a.hbm_slot + t);
-                rec[j] = __ldg(a.record + t);
-                const int64_t lb = static_cast<int64_t>(t) / a.bs;
-                if (lb < a.bt_len) btv[j] = __ldg(a.block_table + lb);
-            } else {
-                bits |= ASU_ST_BAD_QUERY;
-            }
-        }
-    }
-    {
-        const int4 m1 = make_int4(-1, -1, -1, -1);
-        const uint32_t S4 = Sp / 4;
-        for (uint32_t i = tid; i < S4; i += kThreads) reinterpret_cast<int4*>(s_last)[i] = m1;
-        const int4 big = make_int4(INT32_MAX, INT32_MAX, INT32_MAX, INT32_MAX);
-        for (uint32_t i = tid; i < H / 4; i += kThreads) {
-            reinterpret_cast<int4*>(s_hkey)[i] = m1;
-            reinterpret_cast<int4*>(s_hpos)[i] = big;
-        }
-    }
-    if (tid == 0) {
-        n_hits = 0;
-        n_valid = 0;
-    }
-    if (free0 < 0 || free0 > static_cast<int32_t>(S)) {  // uniform across the block
-        if (tid == 0) flag_status(a.status, 0, ASU_ST_BAD_STATE | bits);
+    if (free0 < 0 || free0 > static_cast<int32_t>(S)) {  // uniform across the cluster
+        if (leader && tid == 0) flag_status(a.status, 0, ASU_ST_BAD_STATE);
+        cluster_wait();
         return;
     }
     const int32_t resident0 = static_cast<int32_t>(S) - free0;
@@ -207,15 +193,131 @@ __global__ void __launch_bounds__(kThreads) resolve_lru_kernel(const LruResolveA
     int32_t E = 0;
     if (free0 < tgt) E = (tgt - free0) < resident0 ? (tgt - free0) : resident0;
     const int32_t free1 = free0 + E;
-    __syncthreads();
 
-    // ---- P1: evict lru_order[0, E): mark, read the owners and their records, restore ----
-    for (int32_t k = tid; k < E; k += kThreads) {
-        const int32_t v = s_order[k];
-        int32_t vt = kNotFound;
+    // the leader's own top-k entries and order row, issued first
+    int32_t tok[IPT_Q];
+    constexpr int kVec = (IPT_S + 3) / 4;
+    int4 ov[kVec];
+    const bool vec_row = (S % 4 == 0) && (reinterpret_cast<uintptr_t>(a.order) % 16 == 0);
+    if (leader) {
+#pragma unroll
+        for (int j = 0; j < IPT_Q; ++j) {
+            const uint32_t pos = tid * IPT_Q + j;
+            tok[j] = -1;
+            if (pos < Q) {
+                const int32_t t = __ldg(a.topk + pos);
+                if (t >= 0 && t < a.limit) tok[j] = t;
+            }
+        }
+        if (vec_row) {
+            const int4* src = reinterpret_cast<const int4*>(a.order);
+#pragma unroll
+            for (int j = 0; j < kVec; ++j)
+                if (tid + j * kThreads < S / 4) ov[j] = __ldcg(src + tid + j * kThreads);
+        }
+    }
+    // gathers: entry e of this CTA's eighth -> (state, slot, source) in the leader's shared memory
+    {
+        const uint32_t per = (Q + kCluster - 1) / kCluster;  // <= 512 < kThreads
+        const uint32_t e = crank * per + tid;
+        const bool mine = static_cast<uint32_t>(tid) < per && e < Q;
+        int32_t code = (kCatBad << 16) | kCodeBadSlot, src = -1;
+        if (mine) {
+            const int32_t t = __ldg(a.topk + e);
+            if (t >= 0 && t < a.limit) {
+                const int32_t st = ld_cg(a.token_state + t);
+                const int32_t hs = ld_cg(a.hbm_slot + t);
+                const int32_t rec = __ldg(a.record + t);
+                int32_t tail = -1;
+                const int64_t lb = static_cast<int64_t>(t) / a.bs;
+                if (lb < a.bt_len) {
+                    const int64_t r = static_cast<int64_t>(__ldg(a.block_table + lb)) * a.bs + static_cast<int64_t>(t) % a.bs;
+                    tail = (r >= 0 && r <= INT32_MAX) ? static_cast<int32_t>(r) : -1;
+                }
+                // the source should the entry miss: a record for ASU_ONLY, the paged-cache row for
+                // TAIL_HBM; a resident token evicted by this call takes the state its eviction
+                // restores (ASU_ONLY with a record address, else TAIL_HBM)
+                const int32_t cat = st == ASU_TOKEN_ASU_ONLY ? 0 : st == ASU_TOKEN_HBM_RESIDENT ? 1
+                                    : st == ASU_TOKEN_TAIL_HBM ? 2 : kCatBad;
+                src = cat == 0 ? rec : cat == 2 ? tail : (rec >= 0 ? rec : tail);
+                code = (cat << 16) | (static_cast<uint32_t>(hs) < S ? hs : kCodeBadSlot);
+            }
+        }
+        cluster_wait();  // every CTA has started
+        if (mine) {
+            cluster.map_shared_rank(g_code, 0)[e] = code;
+            cluster.map_shared_rank(g_src, 0)[e] = src;
+        }
+    }
+    // victims lru_order[0, E): position k belongs to thread k / kCluster of CTA k % kCluster, and
+    // a second one to the same thread at k + kCluster * kThreads (E <= 16384).  They are marked
+    // now in the leader's last_pos table and restored after the first cluster barrier (the
+    // gathers above read the token states unchanged).  The first one's slot and owner stay in
+    // registers; the rare second one is read again after the barrier.
+    const int32_t ct = tid * kCluster + static_cast<int32_t>(crank);
+    constexpr int32_t kSpan = kCluster * kThreads;
+    int32_t vslot = kNotFound, vtok = kNotFound;
+    if (ct < E) {
+        vslot = ld_cg(a.order + ct);
+        if (static_cast<uint32_t>(vslot) < S) {
+            cluster.map_shared_rank(s_last, 0)[vslot] = kVictim;
+            vtok = ld_cg(a.owner + vslot);
+        } else {
+            bits |= ASU_ST_BAD_STATE;
+        }
+    }
+    if (ct + kSpan < E) {
+        const int32_t v = ld_cg(a.order + ct + kSpan);
+        if (static_cast<uint32_t>(v) < S) cluster.map_shared_rank(s_last, 0)[v] = kVictim;
+        else bits |= ASU_ST_BAD_STATE;
+    }
+    if (leader) {
+        // the order row into shared memory, last_pos of the surviving residents, the hash
+        if (vec_row) {
+            int4* dst = reinterpret_cast<int4*>(s_order);
+#pragma unroll
+            for (int j = 0; j < kVec; ++j) {
+                const int32_t i4 = tid + j * kThreads;
+                if (i4 >= static_cast<int32_t>(S / 4)) continue;
+                dst[i4] = ov[j];
+                const int32_t v[4] = {ov[j].x, ov[j].y, ov[j].z, ov[j].w};
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const int32_t k = 4 * i4 + c;
+                    if (k >= E && k < resident0 && static_cast<uint32_t>(v[c]) < S) s_last[v[c]] = -1;
+                }
+            }
+        } else {
+            for (int32_t k = tid; k < static_cast<int32_t>(S); k += kThreads) {
+                const int32_t v = ld_cg(a.order + k);
+                s_order[k] = v;
+                if (k >= E && k < resident0 && static_cast<uint32_t>(v) < S) s_last[v] = -1;
+            }
+        }
+        const int4 m1 = make_int4(-1, -1, -1, -1);
+        const int4 big = make_int4(INT32_MAX, INT32_MAX, INT32_MAX, INT32_MAX);
+        for (uint32_t i = tid; i < H / 4; i += kThreads) {
+            reinterpret_cast<int4*>(s_hkey)[i] = m1;
+            reinterpret_cast<int4*>(s_hpos)[i] = big;
+            reinterpret_cast<int4*>(s_hmax)[i] = m1;
+        }
+        if (tid == 0) {
+            n_hits = 0;
+            n_valid = 0;
+            if (a.ev_count) *a.ev_count = E;
+        }
+    }
+    cluster_arrive();
+    cluster_wait();  // A: gathers, victim marks, order row and hash in place
+
+    // ---- restores (every CTA: its victims) | classification (leader) ----
+    for (int32_t k = ct; k < E; k += kSpan) {
+        int32_t v = vslot, vt = vtok;
+        if (k != ct) {  // the second victim of this thread
+            v = ld_cg(a.order + k);
+            vt = static_cast<uint32_t>(v) < S ? ld_cg(a.owner + v) : kNotFound;
+        }
         if (static_cast<uint32_t>(v) < S) {
-            s_last[v] = kVictim;
-            vt = ld_cg(a.owner + v);
             if (vt >= 0 && vt < a.max_seq) {
                 const int32_t vr = __ldg(a.record + vt);
                 st_cg(a.token_state + vt, vr >= 0 ? ASU_TOKEN_ASU_ONLY : ASU_TOKEN_TAIL_HBM);
@@ -225,226 +327,242 @@ __global__ void __launch_bounds__(kThreads) resolve_lru_kernel(const LruResolveA
             }
             st_cg(a.owner + v, kNotFound);
             st_cg(a.stack + free0 + k, v);
-        } else {
-            bits |= ASU_ST_BAD_STATE;
         }
-        if (a.evicted) a.evicted[k] = vt;
+        if (a.evicted) a.evicted[k] = static_cast<uint32_t>(v) < S ? vt : kNotFound;
     }
-    if (tid == 0 && a.ev_count) *a.ev_count = E;
-    __syncthreads();  // victim marks visible; restores ordered before any install
-
-    // ---- P2: classify; hits record their position, misses claim the hash ----
     uint8_t cls[IPT_Q];
-    int32_t hidx[IPT_Q], src[IPT_Q];
+    int32_t hidx[IPT_Q], src[IPT_Q], hs[IPT_Q];
     int valid_local = 0;
+    if (leader) {
 #pragma unroll
-    for (int j = 0; j < IPT_Q; ++j) {
-        const int32_t pos = tid * IPT_Q + j;
-        cls[j] = kNone;
-        hidx[j] = -1;
-        src[j] = -1;
-        if (tok[j] < 0) continue;
-        ++valid_local;
-        int32_t state = st[j];
-        if (state == ASU_TOKEN_HBM_RESIDENT) {
-            const int32_t s = hs[j];
-            if (static_cast<uint32_t>(s) >= S) {
-                bits |= ASU_ST_BAD_STATE;
+        for (int j = 0; j < IPT_Q; ++j) {
+            const int32_t pos = tid * IPT_Q + j;
+            cls[j] = kNone;
+            hidx[j] = -1;
+            src[j] = -1;
+            hs[j] = kNotFound;
+            if (static_cast<uint32_t>(pos) < Q && tok[j] < 0) bits |= ASU_ST_BAD_QUERY;
+            if (tok[j] < 0) continue;
+            ++valid_local;
+            const int32_t code = g_code[pos];
+            const int32_t cat = code >> 16;
+            const int32_t s = code & 0xffff;
+            src[j] = g_src[pos];
+            if (cat == 1) {
+                if (s == kCodeBadSlot) {
+                    bits |= ASU_ST_BAD_STATE;
+                    continue;
+                }
+                if (s_last[s] != kVictim) {
+                    cls[j] = kHit;
+                    hs[j] = s;
+                    atomicMax(&s_last[s], pos);
+                    continue;
+                }
+                // evicted by this call: a miss from the source its restored state names
+            } else if (cat == kCatBad) {
+                bits |= ASU_ST_BAD_TOKEN_STATE;
                 continue;
             }
-            if (s_last[s] != kVictim) {
-                cls[j] = kHit;
-                atomicMax(&s_last[s], pos);
+            if (src[j] < 0 || src[j] >= a.src_rows) {
+                bits |= ASU_ST_BAD_SOURCE;  // skipped: the reference raises here
                 continue;
             }
-            state = rec[j] >= 0 ? ASU_TOKEN_ASU_ONLY : ASU_TOKEN_TAIL_HBM;  // evicted in this call
-        }
-        if (state == ASU_TOKEN_ASU_ONLY) {
-            src[j] = rec[j];
-        } else if (state == ASU_TOKEN_TAIL_HBM) {
-            if (static_cast<int64_t>(tok[j]) / a.bs < a.bt_len) {  // else the block table does not cover it
-                const int64_t r = static_cast<int64_t>(btv[j]) * a.bs + static_cast<int64_t>(tok[j]) % a.bs;
-                src[j] = (r >= 0 && r <= INT32_MAX) ? static_cast<int32_t>(r) : -1;
+            cls[j] = kMiss;
+            uint32_t h = hash_key(tok[j], a.log2h);
+            while (true) {  // terminates: at most Q <= H distinct tokens
+                const int32_t old = atomicCAS(&s_hkey[h], kEmptyKey, tok[j]);
+                if (old == kEmptyKey || old == tok[j]) break;
+                h = (h + 1) & (H - 1);
             }
-        } else {
-            bits |= ASU_ST_BAD_TOKEN_STATE;
-            continue;
+            hidx[j] = static_cast<int32_t>(h);
+            atomicMin(&s_hpos[h], pos);  // the first position installs
+            atomicMax(&s_hmax[h], pos);  // the last one is its slot's last touch
         }
-        if (src[j] < 0 || src[j] >= a.src_rows) {
-            bits |= ASU_ST_BAD_SOURCE;  // skipped: the reference raises here
-            continue;
-        }
-        cls[j] = kMiss;
-        uint32_t h = hash_key(tok[j], a.log2h);
-        while (true) {  // terminates: at most Q <= H distinct tokens
-            const int32_t old = atomicCAS(&s_hkey[h], kEmptyKey, tok[j]);
-            if (old == kEmptyKey || old == tok[j]) break;
-            h = (h + 1) & (H - 1);
-        }
-        hidx[j] = static_cast<int32_t>(h);
-        atomicMin(&s_hpos[h], pos);
     }
-    __syncthreads();  // every claim made
+    cluster_arrive();
+    cluster_wait();  // A2: every claim made; restores ordered before any install
 
-    // ---- P3: first occurrences pop the stack in top-k order and install ----
-    int canon[IPT_Q];
-    int local = 0;
+    int32_t n_inst = 0;
+    if (leader) {
+        // ---- P3: first occurrences pop the stack in top-k order and install ----
+        int canon[IPT_Q];
+        int local = 0;
 #pragma unroll
-    for (int j = 0; j < IPT_Q; ++j) {
-        canon[j] = cls[j] == kMiss && s_hpos[hidx[j]] == static_cast<int32_t>(tid * IPT_Q + j);
-        local += canon[j];
-    }
-    int n_canon = 0;
-    int rank = block_exclusive_scan_1b(local, scan_a, &n_canon);
-    int32_t slot[IPT_Q];
+        for (int j = 0; j < IPT_Q; ++j) {
+            canon[j] = cls[j] == kMiss && s_hpos[hidx[j]] == static_cast<int32_t>(tid * IPT_Q + j);
+            local += canon[j];
+        }
+        int n_canon = 0;
+        int rank = block_exclusive_scan_1b(local, scan_a, &n_canon);
+        int32_t slot[IPT_Q];
 #pragma unroll
-    for (int j = 0; j < IPT_Q; ++j) {
-        slot[j] = cls[j] == kHit ? hs[j] : kNotFound;
-        if (!canon[j]) continue;
-        const int32_t pos = tid * IPT_Q + j;
-        const int32_t k = rank++;
-        int32_t s = kNotFound;
-        if (k < free1) {
-            // the victims just pushed (top first), then the older entries below them
-            s = k < E ? s_order[E - 1 - k] : ld_cg(a.stack + (free0 - 1 - (k - E)));
-            if (static_cast<uint32_t>(s) >= S) {
-                bits |= ASU_ST_BAD_STATE;
-                s = kNotFound;
+        for (int j = 0; j < IPT_Q; ++j) {
+            slot[j] = cls[j] == kHit ? hs[j] : kNotFound;
+            if (!canon[j]) continue;
+            const int32_t k = rank++;
+            int32_t s = kNotFound;
+            if (k < free1) {
+                // the victims just pushed (top first), then the older entries below them
+                s = k < E ? s_order[E - 1 - k] : ld_cg(a.stack + (free0 - 1 - (k - E)));
+                if (static_cast<uint32_t>(s) >= S) {
+                    bits |= ASU_ST_BAD_STATE;
+                    s = kNotFound;
+                }
+            } else {
+                bits |= ASU_ST_FREE_EXHAUSTED;
             }
-        } else {
-            bits |= ASU_ST_FREE_EXHAUSTED;
-        }
-        s_hval[hidx[j]] = s;
-        if (k < free1) {
-            s_isrc[k] = s >= 0 ? src[j] : -1;
-            s_islot[k] = s;
-        }
-        if (s >= 0) {
-            st_cg(a.token_state + tok[j], ASU_TOKEN_HBM_RESIDENT);
-            st_cg(a.hbm_slot + tok[j], s);
-            st_cg(a.owner + s, tok[j]);
-            atomicMax(&s_last[s], pos);
-        }
-        slot[j] = s;
-    }
-    const int32_t n_inst = n_canon < free1 ? n_canon : free1;
-    const int32_t free2 = free1 - n_inst;
-    __syncthreads();
-
-    // ---- P4: later duplicates of a missing token, outputs ----
-    int hits_local = 0;
-#pragma unroll
-    for (int j = 0; j < IPT_Q; ++j) {
-        const int32_t pos = tid * IPT_Q + j;
-        bool hit = cls[j] == kHit;
-        if (cls[j] == kMiss && !canon[j]) {
-            const int32_t v = s_hval[hidx[j]];
-            if (v >= 0) {
-                slot[j] = v;
-                hit = true;
-                atomicMax(&s_last[v], pos);
+            s_hval[hidx[j]] = s;
+            if (k < free1) {
+                s_isrc[k] = s >= 0 ? src[j] : -1;
+                s_islot[k] = s;
             }
+            if (s >= 0) {
+                st_cg(a.token_state + tok[j], ASU_TOKEN_HBM_RESIDENT);
+                st_cg(a.hbm_slot + tok[j], s);
+                st_cg(a.owner + s, tok[j]);
+                s_last[s] = s_hmax[hidx[j]];  // only this thread touches a popped slot before the barrier
+            }
+            slot[j] = s;
         }
-        hits_local += hit;
-        if (static_cast<uint32_t>(pos) < Q) a.resolved[pos] = slot[j];
-    }
-    hits_local = __reduce_add_sync(0xffffffffu, hits_local);
-    valid_local = __reduce_add_sync(0xffffffffu, valid_local);
-    if ((tid & 31) == 0) {
-        if (hits_local) atomicAdd(&n_hits, hits_local);
-        if (valid_local) atomicAdd(&n_valid, valid_local);
-    }
-    __syncthreads();
+        n_inst = n_canon < free1 ? n_canon : free1;
+        const int32_t free2 = free1 - n_inst;
+        if (tid == 0) s_ninst = n_inst;
+        __syncthreads();  // installed slots, their last touches and the install list in place
+        cluster_arrive();  // B: the other CTAs copy the rows while the leader reorders
 
-    // ---- P5: new recency order ----
-    int32_t oldv[IPT_S];
-    bool keep[IPT_S];
-    int keep_local = 0;
-    if (tid * IPT_S < static_cast<int>(Sp)) {
-        if constexpr (IPT_S % 4 == 0) {
+        // ---- P4: later duplicates of a missing token, outputs ----
+        int hits_local = 0;
 #pragma unroll
-            for (int j = 0; j < IPT_S; j += 4) {
-                const int4 v4 = reinterpret_cast<const int4*>(s_order)[(tid * IPT_S + j) / 4];
-                oldv[j] = v4.x;
-                oldv[j + 1] = v4.y;
-                oldv[j + 2] = v4.z;
-                oldv[j + 3] = v4.w;
+        for (int j = 0; j < IPT_Q; ++j) {
+            const int32_t pos = tid * IPT_Q + j;
+            bool hit = cls[j] == kHit;
+            if (cls[j] == kMiss && !canon[j]) {
+                const int32_t v = s_hval[hidx[j]];
+                if (v >= 0) {
+                    slot[j] = v;
+                    hit = true;
+                }
+            }
+            hits_local += hit;
+            if (static_cast<uint32_t>(pos) < Q) a.resolved[pos] = slot[j];
+        }
+        hits_local = __reduce_add_sync(0xffffffffu, hits_local);
+        valid_local = __reduce_add_sync(0xffffffffu, valid_local);
+        if ((tid & 31) == 0) {
+            if (hits_local) atomicAdd(&n_hits, hits_local);
+            if (valid_local) atomicAdd(&n_valid, valid_local);
+        }
+
+        // ---- P5: new recency order ----
+        int32_t oldv[IPT_S];
+        bool keep[IPT_S];
+        int keep_local = 0;
+        if (tid * IPT_S < static_cast<int>(Sp)) {
+            if constexpr (IPT_S % 4 == 0) {
+#pragma unroll
+                for (int j = 0; j < IPT_S; j += 4) {
+                    const int4 v4 = reinterpret_cast<const int4*>(s_order)[(tid * IPT_S + j) / 4];
+                    oldv[j] = v4.x;
+                    oldv[j + 1] = v4.y;
+                    oldv[j + 2] = v4.z;
+                    oldv[j + 3] = v4.w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < IPT_S; ++j) oldv[j] = s_order[tid * IPT_S + j];
             }
         } else {
 #pragma unroll
-            for (int j = 0; j < IPT_S; ++j) oldv[j] = s_order[tid * IPT_S + j];
+            for (int j = 0; j < IPT_S; ++j) oldv[j] = -1;
         }
+#pragma unroll
+        for (int j = 0; j < IPT_S; ++j) {
+            const int32_t idx = tid * IPT_S + j;
+            const bool live = idx >= E && idx < resident0;
+            keep[j] = live && static_cast<uint32_t>(oldv[j]) < S && s_last[oldv[j]] == -1;
+            if (live && static_cast<uint32_t>(oldv[j]) >= S) bits |= ASU_ST_BAD_STATE;
+            keep_local += keep[j];
+        }
+        bool touched[IPT_Q];
+        int touched_local = 0;
+#pragma unroll
+        for (int j = 0; j < IPT_Q; ++j) {
+            touched[j] = slot[j] >= 0 && s_last[slot[j]] == static_cast<int32_t>(tid * IPT_Q + j);
+            touched_local += touched[j];
+        }
+        int packed_total = 0;  // kept residents in the low 16 bits (<= S), touched slots above (<= Q)
+        const int packed = block_exclusive_scan_1b(keep_local | (touched_local << 16), scan_b, &packed_total);
+        int ka = packed & 0xffff;
+        int kb = packed >> 16;
+        const int n_keep = packed_total & 0xffff;
+        const int n_touched = packed_total >> 16;
+#pragma unroll
+        for (int j = 0; j < IPT_S; ++j) {
+            if (keep[j]) {
+                if (ka < static_cast<int>(S)) s_order[ka] = oldv[j];
+                ++ka;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < IPT_Q; ++j) {
+            if (touched[j]) {
+                const int o = n_keep + kb++;
+                if (o < static_cast<int>(S)) s_order[o] = slot[j];
+            }
+        }
+        __syncthreads();
+        const int n_new = min(n_keep + n_touched, static_cast<int>(S));
+        if (vec_row) {
+            const int n4 = n_new / 4;
+            for (int i = tid; i < n4; i += kThreads)
+                __stcg(reinterpret_cast<int4*>(a.order) + i, reinterpret_cast<const int4*>(s_order)[i]);
+            for (int i = n4 * 4 + tid; i < n_new; i += kThreads) st_cg(a.order + i, s_order[i]);
+        } else {
+            for (int i = tid; i < n_new; i += kThreads) st_cg(a.order + i, s_order[i]);
+        }
+        if (tid == 0) {
+            st_cg(a.count, free2);
+            if (n_keep + n_touched != static_cast<int>(S) - free2) bits |= ASU_ST_BAD_STATE;
+            if (a.stats != nullptr) {
+                unsigned long long* row = reinterpret_cast<unsigned long long*>(a.stats);
+                atomicAdd(row + ASU_LRU_STAT_HITS, static_cast<unsigned long long>(n_hits));
+                atomicAdd(row + ASU_LRU_STAT_MISSES, static_cast<unsigned long long>(n_valid - n_hits));
+                atomicAdd(row + ASU_LRU_STAT_INSTALLS, static_cast<unsigned long long>(n_inst));
+                atomicAdd(row + ASU_LRU_STAT_SHORTAGES, static_cast<unsigned long long>(n_valid - n_hits - n_inst));
+                atomicAdd(row + ASU_LRU_STAT_EVICTIONS, static_cast<unsigned long long>(E));
+            }
+        }
+        cluster_wait();  // B
     } else {
-#pragma unroll
-        for (int j = 0; j < IPT_S; ++j) oldv[j] = -1;
-    }
-#pragma unroll
-    for (int j = 0; j < IPT_S; ++j) {
-        const int32_t idx = tid * IPT_S + j;
-        const bool live = idx >= E && idx < resident0;
-        keep[j] = live && static_cast<uint32_t>(oldv[j]) < S && s_last[oldv[j]] == -1;
-        if (live && static_cast<uint32_t>(oldv[j]) >= S) bits |= ASU_ST_BAD_STATE;
-        keep_local += keep[j];
-    }
-    bool touched[IPT_Q];
-    int touched_local = 0;
-#pragma unroll
-    for (int j = 0; j < IPT_Q; ++j) {
-        touched[j] = slot[j] >= 0 && s_last[slot[j]] == static_cast<int32_t>(tid * IPT_Q + j);
-        touched_local += touched[j];
-    }
-    int packed_total = 0;  // kept residents in the low 16 bits (<= S), touched slots above (<= Q)
-    const int packed = block_exclusive_scan_1b(keep_local | (touched_local << 16), scan_b, &packed_total);
-    int ka = packed & 0xffff;
-    int kb = packed >> 16;
-    const int n_keep = packed_total & 0xffff;
-    const int n_touched = packed_total >> 16;
-#pragma unroll
-    for (int j = 0; j < IPT_S; ++j) {
-        if (keep[j]) {
-            if (ka < static_cast<int>(S)) s_order[ka] = oldv[j];
-            ++ka;
+        cluster_arrive();
+        cluster_wait();  // B: the install list is complete
+        // ---- P6 (CTAs 1..7): the installed row pairs ----
+        // An unusable pop (bad slot) is listed with source -1 and copied by nobody.
+        n_inst = *cluster.map_shared_rank(&s_ninst, 0);
+        const int32_t* l_src = cluster.map_shared_rank(s_isrc, 0);
+        const int32_t* l_slot = cluster.map_shared_rank(s_islot, 0);
+        int32_t* c_src = smem;       // this CTA's copy of the list
+        int32_t* c_slot = smem + Qp;
+        for (int i = tid; i < n_inst; i += kThreads) {
+            c_src[i] = l_src[i];
+            c_slot[i] = l_slot[i];
         }
+        __syncthreads();
+        const uint32_t first = (crank - 1) * kThreads + tid, threads = (kCluster - 1) * kThreads;
+        if (a.vec == 16)
+            copy_rows<int4>(c_src, c_slot, n_inst, a.kv0_src, a.kv1_src, a.kv0_dst, a.kv1_dst, a.c0, a.c1, first,
+                            threads);
+        else if (a.vec == 4)
+            copy_rows<int32_t>(c_src, c_slot, n_inst, a.kv0_src, a.kv1_src, a.kv0_dst, a.kv1_dst, a.c0, a.c1, first,
+                               threads);
+        else if (a.vec == 1)
+            copy_rows<uint8_t>(c_src, c_slot, n_inst, a.kv0_src, a.kv1_src, a.kv0_dst, a.kv1_dst, a.c0, a.c1, first,
+                               threads);
     }
-#pragma unroll
-    for (int j = 0; j < IPT_Q; ++j) {
-        if (touched[j]) {
-            const int o = n_keep + kb++;
-            if (o < static_cast<int>(S)) s_order[o] = slot[j];
-        }
-    }
-    __syncthreads();
-    const int n_new = min(n_keep + n_touched, static_cast<int>(S));
-    if (vec_row) {
-        const int n4 = n_new / 4;
-        for (int i = tid; i < n4; i += kThreads)
-            __stcg(reinterpret_cast<int4*>(a.order) + i, reinterpret_cast<const int4*>(s_order)[i]);
-        for (int i = n4 * 4 + tid; i < n_new; i += kThreads) st_cg(a.order + i, s_order[i]);
-    } else {
-        for (int i = tid; i < n_new; i += kThreads) st_cg(a.order + i, s_order[i]);
-    }
-    if (tid == 0) {
-        st_cg(a.count, free2);
-        if (n_keep + n_touched != static_cast<int>(S) - free2) bits |= ASU_ST_BAD_STATE;
-        if (a.stats != nullptr) {
-            unsigned long long* row = reinterpret_cast<unsigned long long*>(a.stats);
-            atomicAdd(row + ASU_LRU_STAT_HITS, static_cast<unsigned long long>(n_hits));
-            atomicAdd(row + ASU_LRU_STAT_MISSES, static_cast<unsigned long long>(n_valid - n_hits));
-            atomicAdd(row + ASU_LRU_STAT_INSTALLS, static_cast<unsigned long long>(n_inst));
-            atomicAdd(row + ASU_LRU_STAT_SHORTAGES, static_cast<unsigned long long>(n_valid - n_hits - n_inst));
-            atomicAdd(row + ASU_LRU_STAT_EVICTIONS, static_cast<unsigned long long>(E));
-        }
-    }
-
-    // ---- P6: the installed row pairs (the list was complete at P3's barrier) ----
-    // An unusable pop (bad slot) is listed with source -1 and copied by nobody.
-    if (a.vec == 16)
-        copy_rows<int4>(s_isrc, s_islot, n_inst, a.kv0_src, a.kv1_src, a.kv0_dst, a.kv1_dst, a.c0, a.c1);
-    else if (a.vec == 4)
-        copy_rows<int32_t>(s_isrc, s_islot, n_inst, a.kv0_src, a.kv1_src, a.kv0_dst, a.kv1_dst, a.c0, a.c1);
-    else if (a.vec == 1)
-        copy_rows<uint8_t>(s_isrc, s_islot, n_inst, a.kv0_src, a.kv1_src, a.kv0_dst, a.kv1_dst, a.c0, a.c1);
     if (bits) flag_status(a.status, 0, bits);
+    cluster_arrive();
+    cluster_wait();  // C: the leader's shared memory stays until every CTA has read the list
 }
 
 inline uint32_t pow2ceil(uint32_t x) {
@@ -453,7 +571,8 @@ inline uint32_t pow2ceil(uint32_t x) {
     return p;
 }
 
-// Dynamic shared memory: order + last_pos rows, the hash table and the install list.
+// Dynamic shared memory of every CTA (the leader's layout): order + last_pos rows, the hash table
+// (three arrays) and the gathered entries (two arrays, later the install list).
 inline size_t smem_bytes(uint32_t S, uint32_t Q, int* log2h_out) {
     const uint64_t Sp = (S + 3) & ~3u;
     const uint64_t Qp = (Q + 3) & ~3u;
@@ -476,7 +595,7 @@ int launch(cudaStream_t s, LruResolveArgs a) {
     const int rc = asu_max_dynamic_smem(reinterpret_cast<const void*>(resolve_lru_kernel<IPT_Q, IPT_S>), &max_dynamic);
     if (rc != ASU_OK) return rc;
     if (smem > static_cast<size_t>(max_dynamic)) return ASU_ERR_ARG;
-    return launch_pdl(resolve_lru_kernel<IPT_Q, IPT_S>, dim3(1), dim3(kThreads), smem, s, a);
+    return launch_pdl(resolve_lru_kernel<IPT_Q, IPT_S>, dim3(kCluster), dim3(kThreads), smem, s, a);
 }
 
 template <int IPT_Q>

@@ -130,8 +130,8 @@ def parse_args():
     p.add_argument("--no-balance", action="store_true",
                    help="resolver workloads on N > 1 GPUs: no swap-in balancing between ranks")
     p.add_argument("--balance-share", type=int, default=0,
-                   help="N > 1: skip the calibration and let rank 1 swap in the last M requests of rank 0 "
-                        "(a fixed plan for checking the balanced path)")
+                   help="N > 1: start from a plan in which rank 1 swaps in the last M requests of rank 0 "
+                        "(skips the unbalanced calibration round; checks the balanced path on any box)")
     p.add_argument("--shared-pool", action="store_true",
                    help="1 GPU: back the host pool with a shared-memory file registered with the GPU "
                         "(the pool every rank uses on N > 1 GPUs) instead of cudaHostAlloc")
@@ -460,7 +460,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
         r0, R = rank * cfg.req, cfg.req
     K_steps, W, L = args.steps, args.warmup, cfg.layers
     balance = world > 1 and not args.no_balance
-    cal = 0 if not balance or args.balance_share else CAL_STEPS * (1 + CAL_ROUNDS)
+    cal = 0 if not balance else CAL_STEPS * (CAL_ROUNDS + (0 if args.balance_share else 1))
     base = args.prefill + cal + W
     cpu_leg = world == 1 and not args.no_cpu_baseline and cfg.name == "resolver"
     n_steps = base + (max(2 * K_steps, CPU_CYCLE_STEPS) if cpu_leg else 2 * K_steps)
@@ -511,44 +511,48 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     balance_info = None
     if bal is not None:
         rank_sync(torch)
-        if args.balance_share:
-            bal.set_plan([(0, 1, args.balance_share)])
-            balance_info = {"pairs": [[0, 1, args.balance_share]], "fixed": True}
-        else:
-            done = [args.prefill]
+        done = [args.prefill]
 
-            def cal_steps(n):
-                run_steps(done[0], n)
-                done[0] += n
+        def cal_steps(n):
+            run_steps(done[0], n)
+            done[0] += n
 
-            balance_info = bal.calibrate(cal_steps, steps=CAL_STEPS, rounds=CAL_ROUNDS)
-    run_steps(args.prefill + cal, W)  # untimed warm-up
-    rank_sync(torch)
-
+        balance_info = bal.calibrate(cal_steps, steps=CAL_STEPS, rounds=CAL_ROUNDS,
+                                     initial_pairs=[(0, 1, args.balance_share)] if args.balance_share else None)
     # per step and layer: [a] resolve [b] swap-in [c]; the free-count snapshots sit outside
     ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(L)] for _ in range(K_steps)]
-    free_before = torch.empty(K_steps * L, dtype=torch.int64, device=dev)
-    free_after = torch.empty(K_steps * L, dtype=torch.int64, device=dev)
-    evicting = torch.empty(K_steps * L, dtype=torch.int64, device=dev)  # request-steps that evicted
+    ev_warm = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(L)] for _ in range(W)]
+    free_before = torch.empty(max(K_steps, W) * L, dtype=torch.int64, device=dev)
+    free_after = torch.empty(max(K_steps, W) * L, dtype=torch.int64, device=dev)
+    evicting = torch.empty(max(K_steps, W) * L, dtype=torch.int64, device=dev)  # request-steps that evicted
+    # the device idles in this spin while the host queues the step (longer when the step also
+    # queues the balancing's NCCL messages), so host time stays out of the timed intervals
+    spin = 100_000 if bal is None else 400_000
+
+    def timed_steps(first, events):
+        for k, step_ev in enumerate(events):
+            flush()
+            torch.cuda._sleep(spin)
+            for layer in range(L):
+                o = outs[(k * L + layer) % 2]
+                free_before[k * L + layer] = pools[layer].free_count.sum()
+                q = q_dev[first + k, layer]
+                a, b, c = step_ev[layer]
+                a.record()
+                pools[layer].step(q, out=o)
+                b.record()
+                swapin(layer, q, o)
+                c.record()
+                free_after[k * L + layer] = pools[layer].free_count.sum()
+                evicting[k * L + layer] = (o.evicted_count > 0).sum()
+
+    timed_steps(args.prefill + cal, ev_warm)  # untimed warm-up: the timed loop's own code
+    rank_sync(torch)
     stats0 = total_stats().clone()
     clocks = ClockSampler(gpu_index(local_rank))
     clocks.start()
     torch.cuda.synchronize()
-    for k in range(K_steps):
-        flush()
-        torch.cuda._sleep(100_000)  # keep the GPU busy while the host queues the step
-        for layer in range(L):
-            o = outs[(k * L + layer) % 2]
-            free_before[k * L + layer] = pools[layer].free_count.sum()
-            q = q_dev[base + k, layer]
-            a, b, c = ev[k][layer]
-            a.record()
-            pools[layer].step(q, out=o)
-            b.record()
-            swapin(layer, q, o)
-            c.record()
-            free_after[k * L + layer] = pools[layer].free_count.sum()
-            evicting[k * L + layer] = (o.evicted_count > 0).sum()
+    timed_steps(base, ev)
     rank_sync(torch)
     clk = clocks.stop()
     resolve_ms = [a.elapsed_time(b) for step in ev for a, b, _ in step]
@@ -573,7 +577,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     rank_sync(torch)
     for k in range(K_steps):
         flush()
-        torch.cuda._sleep(100_000)
+        torch.cuda._sleep(spin)
         ev2[k][0].record()
         for layer in range(L):
             o = outs[(k * L + layer) % 2]
@@ -665,6 +669,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             "host_cpus_bound": len(bound_cpus),
             "note_step_time": "sum over layers of (resolve + swap-in) event intervals",
             "balance": balance_info,
+            "step_ms_by_rank0": step_ms,
             "verified_rows": verified,
             "cpu_baseline": cpu,
             "clocks": clk,

@@ -7,8 +7,9 @@ with two GPUs, the balanced bench path end to end.
 * ``asu_swapin_gather_to_peer`` (plain 16-byte stores, system fence) into a slot pool on this GPU
   equals the oracle for TMA-sized rows and for block rows.
 * Two GPUs: ``bench.py --gpus 2 --balance-share 32 --verify`` runs rank 1 as the helper of rank 0
-  (NCCL messages, a CUDA IPC mapping of rank 0's slot pool, rank 0's host pool mapped in rank 1)
-  and checks every resident row of every request of both ranks against its host record.
+  (NCCL messages, a CUDA IPC mapping of rank 0's slot pool, rank 0's host pool mapped in rank 1),
+  refines the share from measured steps, and checks every resident row of every request of both
+  ranks against its host record.
 """
 
 import json
@@ -117,5 +118,6 @@ def test_two_gpu_balanced_bench_rows_verified():
     out = subprocess.run(cmd, capture_output=True, text=True, cwd=ROOT, timeout=900, env=env)
     assert out.returncode == 0, out.stderr[-3000:]
     line = json.loads([ln for ln in out.stdout.splitlines() if ln.startswith("{")][-1])
-    assert line["n_gpus"] == 2 and line["balance"]["pairs"] == [[0, 1, 32]]
+    assert line["n_gpus"] == 2 and [p[:2] for p in line["balance"]["pairs"]] == [[0, 1]]
+    assert line["balance"]["history"][0]["pairs"] == [[0, 1, 32]]
     assert line["verified_rows"] > 0
