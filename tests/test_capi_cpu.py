@@ -66,6 +66,15 @@ def test_argument_validation_rejects_before_launch(lib):
     assert L.asu_swapin_gather(None, 8, 10, 32, 0, 1, 1, 1, 1, 1, 4, 16, 4, 1, None) == lib.ASU_ERR_ALIGN
     assert L.asu_swapin_gather(None, 16, 10, 32, 40, 1, 1, 1, 1, 1, 4, 16, 4, 1, None) == lib.ASU_ERR_ALIGN
     assert L.asu_swapin_gather(None, 16, 10, 32, 16, 1, 1, 1, 1, 1, 4, 16, 4, 1, None) == lib.ASU_ERR_ARG
+    # the balancing's entry points: the peer-store swap-in checks like the local one; null
+    # arguments are rejected (or a no-op for the release calls) before any CUDA call
+    assert L.asu_swapin_gather_to_peer(None, 16, 10, 24, 0, 1, 1, 1, 1, 1, 4, 16, 4, 1, None) == lib.ASU_ERR_ALIGN
+    assert L.asu_swapin_gather_to_peer(None, 16, 10, 32, 16, 1, 1, 1, 1, 1, 4, 16, 4, 1, None) == lib.ASU_ERR_ARG
+    assert L.asu_swapin_gather_to_peer(None, 16, 10, 32, 0, 1, 1, 1, 1, 1, 4, 16, 4, 0, None) == lib.ASU_OK
+    assert L.asu_host_register(None, 4096, None) == lib.ASU_ERR_ARG
+    assert L.asu_ipc_export(None, None, None) == lib.ASU_ERR_ARG
+    assert L.asu_ipc_open(None, None) == lib.ASU_ERR_ARG
+    assert L.asu_ipc_close(None) == lib.ASU_OK and L.asu_host_unregister(None) == lib.ASU_OK
     # resolver: block_size 0
     assert L.asu_kv_resolver_do(None, 1, 4, 1, 1, 1, 1, 1, 1, 4, 1, 1, 1, 1, 1, 1, 4, 4, 4, 4, 4, 4, 0, 1, 1,
                                 None) == lib.ASU_ERR_ARG
