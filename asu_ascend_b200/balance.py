@@ -288,7 +288,9 @@ class SwapinBalancer:
         """Choose the pairs and shares.  ``run_steps(n)`` runs n steps of the caller's loop (which
         swaps in through ``self.swapin``); every rank must call this with the same arguments.
         ``initial_pairs`` skips the first round (the unbalanced measurement) and starts the
-        refinement from that plan."""
+        refinement from that plan.  Without it, a last round measures the refined plan, which is
+        kept only if the slowest rank's swap-in got at least 2% faster than with no balancing
+        (otherwise every share goes to 0).  Runs at most ``steps * (rounds + 2)`` steps."""
         req = [int(x) for x in self._gather([float(self.R)])[:, 0].tolist()]
         if initial_pairs is None:
             own, total = self._measure(run_steps, steps)
@@ -309,6 +311,17 @@ class SwapinBalancer:
             self.pairs = [(o, h, refine_share(req[o], req[h], m, g[o, 0].item(), g[h, 1].item()))
                           for o, h, m in self.pairs]
             self._apply_share()
+        if initial_pairs is None and any(m > 0 for _, _, m in self.pairs):
+            # keep the plan only if the slowest rank got faster than with no balancing at all
+            base = max(self.history[0]["ms"])
+            own, total = self._measure(run_steps, steps)
+            g = self._gather([total])
+            kept = max(g[:, 0].tolist()) < 0.98 * base
+            self.history.append({"round": "final", "ms": g[:, 0].tolist(),
+                                 "pairs": [list(p) for p in self.pairs], "kept": kept})
+            if not kept:
+                self.pairs = [(o, h, 0) for o, h, _ in self.pairs]
+                self._apply_share()
         return {"pairs": [list(p) for p in self.pairs], "history": self.history}
 
     def _apply_share(self) -> None:

@@ -460,7 +460,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
         r0, R = rank * cfg.req, cfg.req
     K_steps, W, L = args.steps, args.warmup, cfg.layers
     balance = world > 1 and not args.no_balance
-    cal = 0 if not balance else CAL_STEPS * (CAL_ROUNDS + (0 if args.balance_share else 1))
+    cal = 0 if not balance else CAL_STEPS * (CAL_ROUNDS + (0 if args.balance_share else 2))
     base = args.prefill + cal + W
     cpu_leg = world == 1 and not args.no_cpu_baseline and cfg.name == "resolver"
     n_steps = base + (max(2 * K_steps, CPU_CYCLE_STEPS) if cpu_leg else 2 * K_steps)
