@@ -130,8 +130,8 @@ def parse_args():
     p.add_argument("--no-balance", action="store_true",
                    help="resolver workloads on N > 1 GPUs: no swap-in balancing between ranks")
     p.add_argument("--balance-share", type=int, default=0,
-                   help="N > 1: start from a plan in which rank 1 swaps in the last M requests of rank 0 "
-                        "(skips the unbalanced calibration round; checks the balanced path on any box)")
+                   help="N > 1: start from a plan in which rank N-1-i swaps in the last M requests of rank i "
+                        "for i < N/2 (skips the unbalanced calibration round; checks the balanced path on any box)")
     p.add_argument("--shared-pool", action="store_true",
                    help="1 GPU: back the host pool with a shared-memory file registered with the GPU "
                         "(the pool every rank uses on N > 1 GPUs) instead of cudaHostAlloc")
@@ -518,7 +518,8 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             done[0] += n
 
         balance_info = bal.calibrate(cal_steps, steps=CAL_STEPS, rounds=CAL_ROUNDS,
-                                     initial_pairs=[(0, 1, args.balance_share)] if args.balance_share else None)
+                                     initial_pairs=([(i, world - 1 - i, args.balance_share) for i in range(world // 2)]
+                                                    if args.balance_share else None))
     # per step and layer: [a] resolve [b] swap-in [c]; the free-count snapshots sit outside
     ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(L)] for _ in range(K_steps)]
     ev_warm = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(L)] for _ in range(W)]
