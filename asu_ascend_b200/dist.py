@@ -32,6 +32,18 @@ def reduce_stats(stats: torch.Tensor) -> torch.Tensor:
     return total
 
 
+def rows_by_rank(values: list[float], device: torch.device | str = "cpu") -> list[list[float]]:
+    """Every rank's ``values`` (same length on all ranks), indexed by rank: an end-of-run report
+    of per-rank figures, one all-reduce of a [world, n] tensor holding this rank's row."""
+    if not _initialized():
+        return [list(map(float, values))]
+    world, rank = torch.distributed.get_world_size(), torch.distributed.get_rank()
+    t = torch.zeros((world, len(values)), dtype=torch.float64, device=device)
+    t[rank] = torch.tensor(values, dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.SUM)
+    return t.cpu().tolist()
+
+
 def max_over_ranks(values: list[float], device: torch.device | str = "cpu") -> list[float]:
     """Element-wise max over ranks (timings are reported as the slowest rank's)."""
     t = torch.tensor(values, dtype=torch.float64, device=device)

@@ -446,7 +446,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     import asu_ascend_b200
 
     asu_ascend_b200.load()
-    from asu_ascend_b200.dist import bind_to_gpu_local_cpus, max_over_ranks, reduce_stats, shard_range
+    from asu_ascend_b200.dist import bind_to_gpu_local_cpus, max_over_ranks, reduce_stats, rows_by_rank, shard_range
     from asu_ascend_b200.host_pool import HostRowPool, check_status
     from asu_ascend_b200.lru import LruSlotPools
     from asu_ascend_b200.workloads import record_addresses_torch
@@ -603,6 +603,9 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
         verified = verify_resident_rows(torch, host, recs, pools, slot_pools)
 
     max_ms, max_e2e_ms = max_over_ranks([sum(step_ms), sum(e2e_ms)], dev)  # slowest rank
+    # per rank: its GPU's H2D copy alone and with every rank copying, its timed step and swap-in
+    # intervals and the rows installed into its own requests (every rank takes part)
+    by_rank = rows_by_rank([h2d_alone, h2d_peak, sum(step_ms), sum(swapin_ms), installs], dev)
     job_stats = reduce_stats(torch.stack([p.stats for p in pools])).cpu().tolist()  # end-of-run (NCCL)
     job_req = cfg.req if cfg.strong else cfg.req * world
     idx_per_step = job_req * cfg.topk * L
@@ -670,6 +673,9 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             "host_cpus_bound": len(bound_cpus),
             "note_step_time": "sum over layers of (resolve + swap-in) event intervals",
             "balance": balance_info,
+            "by_rank": [{"h2d_alone_gbs": a, "h2d_concurrent_gbs": c, "step_ms_sum": st, "swapin_ms_sum": sw,
+                         "own_installs": int(n), "own_rows_gbs": n * cfg.row / (sw * 1e-3) / 1e9 if sw > 0 else None}
+                        for a, c, st, sw, n in by_rank],
             "step_ms_by_rank0": step_ms,
             "verified_rows": verified,
             "cpu_baseline": cpu,

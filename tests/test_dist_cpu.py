@@ -10,7 +10,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from asu_ascend_b200.dist import max_over_ranks, reduce_stats, shard_range
+from asu_ascend_b200.dist import max_over_ranks, reduce_stats, rows_by_rank, shard_range
 
 
 def test_shard_range_covers_every_request_once():
@@ -54,7 +54,9 @@ def _worker(rank, world, port, out_path):
         st = _run_rows(trace, list(range(a, b)))
         total = reduce_stats(torch.from_numpy(st))
         slowest = max_over_ranks([float(rank + 1)])
+        rows = rows_by_rank([float(rank), 10.0 * rank + 0.5])
         if rank == 0:
+            assert rows == [[0.0, 0.5], [1.0, 10.5]]
             np.save(out_path, np.concatenate([total.numpy(), np.asarray(slowest, np.int64)]))
     finally:
         dist.destroy_process_group()
