@@ -425,6 +425,21 @@ def rank_sync(torch):
         torch.distributed.barrier()
 
 
+def event_floor_us(torch, flush, spin: int, n: int) -> float:
+    """p50 event interval of a one-element fill timed exactly as a resolve launch is (L2 flush,
+    device spin, event, launch, event): what every such interval holds besides the kernel's work."""
+    tiny = torch.zeros(1, dtype=torch.int32, device=torch.cuda.current_device())
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(max(n, 5))]
+    for a, b in ev:
+        flush()
+        torch.cuda._sleep(spin)
+        a.record()
+        tiny.zero_()
+        b.record()
+    torch.cuda.synchronize()
+    return statistics.median(a.elapsed_time(b) for a, b in ev) * 1e3
+
+
 class L2Flush:
     """Write 256 MiB (evicts everything), then read another 256 MiB so the write-back of dirty lines
     happens here, outside the timed region: the next step starts on a cold, clean L2."""
@@ -593,6 +608,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
         ev2[k][1].record()
     rank_sync(torch)
     e2e_ms = [e[0].elapsed_time(e[1]) for e in ev2]
+    floor_us = event_floor_us(torch, flush, spin, K_steps)
     for p in pools:
         p.check_status()
     check_status(status, "swapin")
@@ -639,6 +655,9 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
         line.update({
             "p50_resolve_us": statistics.median(resolve_ms) * 1e3,
             "mean_resolve_us": statistics.fmean(resolve_ms) * 1e3,
+            # the same event bracket around a one-element fill: the part of every interval that is
+            # the launch and the event pair, whatever the kernel does
+            "event_floor_us": floor_us,
             "p50_swapin_us": statistics.median(swapin_ms) * 1e3,
             "miss_rate": installs / (launches * R * cfg.topk),
             "swapin_gbs": swap_gbs,
