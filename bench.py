@@ -135,6 +135,9 @@ def parse_args():
     p.add_argument("--shared-pool", action="store_true",
                    help="1 GPU: back the host pool with a shared-memory file registered with the GPU "
                         "(the pool every rank uses on N > 1 GPUs) instead of cudaHostAlloc")
+    p.add_argument("--overlap-layers", action="store_true",
+                   help="multi-layer resolver workloads (one GPU or --no-balance): layer l+1's LRU step runs on the "
+                        "main stream while layer l's swap-in runs on a second stream (an A/B of that pipelining)")
     p.add_argument("--verify", action="store_true",
                    help="resolver workloads: after the run, check every resident slot row of every "
                         "request against its host record (GPU-side compare)")
@@ -512,6 +515,53 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
         else:
             host.swapin(recs[layer], q, o.slot, o.install, slot_pools[layer], status=status)
 
+    # Layer pipelining (--overlap-layers): the swap-ins go to a second stream, each after its own
+    # layer's LRU step; the main stream runs the next layer's LRU step meanwhile.  The LRU outputs
+    # (and the e2e query buffer) alternate between two sets, so layer l + 2's step first waits for
+    # layer l's swap-in (and its output copy) to finish reading them.
+    overlap = args.overlap_layers and L > 1
+    if args.overlap_layers and bal is not None:
+        raise SystemExit("--overlap-layers runs the swap-ins locally: use it on one GPU or with --no-balance")
+    main = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev) if overlap else None
+
+    class LayerPipe:
+        """Issues one step's layers serially, or pipelined over the main and the side stream."""
+
+        def __init__(self):
+            self.read_done = [None, None]  # per output set: event after the last reader of it
+
+        def before_step(self, layer):
+            if overlap and layer >= 2:
+                main.wait_event(self.read_done[layer % 2])
+
+        def swapin(self, layer, q, o, after=None, end_event=None, copy_done=None):
+            """Swap in after this layer's step (`after`: an event recorded right after it on the main
+            stream); `end_event` is recorded after the swap-in on its stream."""
+            if not overlap:
+                swapin(layer, q, o)
+                if end_event is not None:
+                    end_event.record(main)
+                return
+            if after is None:
+                after = torch.cuda.Event()
+                after.record(main)
+            side.wait_event(after)
+            with torch.cuda.stream(side):
+                swapin(layer, q, o)
+                if copy_done is not None:
+                    side.wait_event(copy_done)
+                ev = end_event if end_event is not None else torch.cuda.Event(enable_timing=False)
+                ev.record(side)
+            self.read_done[layer % 2] = ev
+
+        def end_step(self):
+            if overlap:
+                main.wait_stream(side)
+                self.read_done = [None, None]
+
+    pipe = LayerPipe()
+
     def total_stats():
         return sum(p.stats.sum(0) for p in pools)
 
@@ -519,8 +569,10 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
         for i in range(first, first + n):
             for layer in range(L):
                 o = outs[(i * L + layer) % 2]
+                pipe.before_step(layer)
                 pools[layer].step(q_dev[i, layer], out=o)
-                swapin(layer, q_dev[i, layer], o)
+                pipe.swapin(layer, q_dev[i, layer], o)
+            pipe.end_step()
 
     run_steps(0, args.prefill)  # untimed: fill the pools
     balance_info = None
@@ -545,35 +597,43 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     # queues the balancing's NCCL messages), so host time stays out of the timed intervals
     spin = 100_000 if bal is None else 400_000
 
-    def timed_steps(first, events):
+    def timed_steps(first, events, brackets):
         for k, step_ev in enumerate(events):
             flush()
             torch.cuda._sleep(spin)
+            brackets[k][0].record()
             for layer in range(L):
                 o = outs[(k * L + layer) % 2]
+                pipe.before_step(layer)
                 free_before[k * L + layer] = pools[layer].free_count.sum()
                 q = q_dev[first + k, layer]
                 a, b, c = step_ev[layer]
                 a.record()
                 pools[layer].step(q, out=o)
                 b.record()
-                swapin(layer, q, o)
-                c.record()
                 free_after[k * L + layer] = pools[layer].free_count.sum()
                 evicting[k * L + layer] = (o.evicted_count > 0).sum()
+                pipe.swapin(layer, q, o, after=b, end_event=c)
+            pipe.end_step()
+            brackets[k][1].record()
 
-    timed_steps(args.prefill + cal, ev_warm)  # untimed warm-up: the timed loop's own code
+    # per step: the whole step, L2 flush and spin excluded (the pipelined step's time)
+    br = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K_steps)]
+    br_warm = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(W)]
+    timed_steps(args.prefill + cal, ev_warm, br_warm)  # untimed warm-up: the timed loop's own code
     rank_sync(torch)
     stats0 = total_stats().clone()
     clocks = ClockSampler(gpu_index(local_rank))
     clocks.start()
     torch.cuda.synchronize()
-    timed_steps(base, ev)
+    timed_steps(base, ev, br)
     rank_sync(torch)
     clk = clocks.stop()
     resolve_ms = [a.elapsed_time(b) for step in ev for a, b, _ in step]
     swapin_ms = [b.elapsed_time(c) for step in ev for _, b, c in step]
-    step_ms = [sum(a.elapsed_time(c) for a, _, c in step) for step in ev]
+    bracket_ms = [a.elapsed_time(b) for a, b in br]
+    # serial: the layers' (resolve + swap-in) intervals; pipelined they overlap, so the step's bracket
+    step_ms = bracket_ms if overlap else [sum(a.elapsed_time(c) for a, _, c in step) for step in ev]
     d_stats = (total_stats() - stats0).cpu().tolist()
     misses, installs, evictions = int(d_stats[1]), int(d_stats[2]), int(d_stats[4])
     n_evicting = int(evicting.sum().item())
@@ -584,12 +644,11 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     base2 = base + K_steps
     slot_host = torch.empty((R, cfg.topk), dtype=torch.int32, pin_memory=True)
     hit_host = torch.empty((R, cfg.topk), dtype=torch.bool, pin_memory=True)
-    q_in = torch.empty((R, cfg.topk), dtype=torch.int32, device=dev)
+    q_ins = [torch.empty((R, cfg.topk), dtype=torch.int32, device=dev) for _ in range(2 if overlap else 1)]
     ev2 = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K_steps)]
     # The slot ids and hit mask go back on a second stream while the swap-in reads host rows:
     # the two copies run in opposite directions of the host link.
     copy_stream = torch.cuda.Stream(dev)
-    main = torch.cuda.current_stream(dev)
     rank_sync(torch)
     for k in range(K_steps):
         flush()
@@ -597,14 +656,23 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
         ev2[k][0].record()
         for layer in range(L):
             o = outs[(k * L + layer) % 2]
+            q_in = q_ins[layer % len(q_ins)]
+            pipe.before_step(layer)
             q_in.copy_(q_host[base2 + k, layer], non_blocking=True)
             pools[layer].step(q_in, out=o)
             copy_stream.wait_stream(main)
             with torch.cuda.stream(copy_stream):
                 slot_host.copy_(o.slot, non_blocking=True)
                 hit_host.copy_(o.hit, non_blocking=True)
-            swapin(layer, q_in, o)
-            main.wait_stream(copy_stream)  # the outputs' buffer is reused two layers later
+            if overlap:
+                copied = torch.cuda.Event()
+                copied.record(copy_stream)
+                pipe.swapin(layer, q_in, o, copy_done=copied)
+            else:
+                swapin(layer, q_in, o)
+                main.wait_stream(copy_stream)  # the outputs' buffer is reused two layers later
+        pipe.end_step()
+        main.wait_stream(copy_stream)
         ev2[k][1].record()
     rank_sync(torch)
     e2e_ms = [e[0].elapsed_time(e[1]) for e in ev2]
@@ -690,7 +758,10 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             "gpu_launches": 2 * launches,
             "job_stats": dict(zip(LruSlotPools.STAT_NAMES, job_stats)),
             "host_cpus_bound": len(bound_cpus),
-            "note_step_time": "sum over layers of (resolve + swap-in) event intervals",
+            "note_step_time": ("the step's event bracket (layers pipelined over two streams)" if overlap else
+                               "sum over layers of (resolve + swap-in) event intervals"),
+            "overlap_layers": overlap,
+            "step_bracket_ms_p50": statistics.median(bracket_ms),
             "balance": balance_info,
             "by_rank": [{"h2d_alone_gbs": a, "h2d_concurrent_gbs": c, "step_ms_sum": st, "swapin_ms_sum": sw,
                          "own_installs": int(n), "own_rows_gbs": n * cfg.row / (sw * 1e-3) / 1e9 if sw > 0 else None}

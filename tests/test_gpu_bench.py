@@ -33,3 +33,27 @@ def test_default_bench_line_carries_the_contract_keys():
     assert e["value"] > 0 and e["h2d_bytes_per_step"] > 0 and e["d2h_bytes_per_step"] > 0
     assert a["gpu_launches"] == 2 * a["steps"]  # one LRU step and one swap-in per timed step
     assert "sm_mhz" in a["clocks"] and "reasons" in a["clocks"]
+
+
+def _bench_line(*args):
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), *args], capture_output=True, text=True, cwd=ROOT,
+                         timeout=900)
+    assert out.returncode == 0, out.stderr[-3000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1
+    return json.loads(lines[0])
+
+
+def test_multilayer_layer_pipelining_keeps_results():
+    """The multi-layer workload with each layer's swap-in on a second stream, overlapping the next
+    layer's LRU step: the same LRU statistics as the serial run of the same trace, and every resident
+    row of every (layer, request) pool equal to its host record afterwards."""
+    common = ["--workload", "multilayer", "--steps", "2", "--warmup", "3", "--prefill", "2", "--no-cpu-baseline",
+              "--verify"]
+    serial = _bench_line(*common)
+    piped = _bench_line(*common, "--overlap-layers")
+    assert serial["overlap_layers"] is False and piped["overlap_layers"] is True
+    assert piped["job_stats"] == serial["job_stats"]
+    assert piped["job_stats"]["installs"] > 0 and piped["job_stats"]["shortages"] == 0
+    assert piped["verified_rows"] == serial["verified_rows"] > 0
+    assert piped["gpu_launches"] == serial["gpu_launches"] == 2 * 2 * 4
