@@ -8,6 +8,8 @@ the CPU tests).
 
 from __future__ import annotations
 
+from typing import Callable
+
 import torch
 
 
@@ -84,3 +86,84 @@ def bind_to_gpu_local_cpus(gpu_index: int, nvml=None) -> list[int]:
         os.sched_setaffinity(0, cpus)
         return cpus
     return []
+
+
+# ------------------------------------------------------------------ rank placement over host links
+
+def host_link_groups(count: int, level: Callable[[int, int], int]) -> list[list[int]]:
+    """Groups of GPUs (ordinals ``0..count-1``) that share a host attachment.
+
+    ``level(i, j)`` is the NVML topology level of the pair's closest common ancestor (10 same board,
+    20 / 30 PCIe switches or one host bridge, 40 same NUMA node, 50 across the system).  GPUs are in
+    one group when their level is below the largest level seen between any two of them, so a box
+    whose GPUs hang off two sockets (or two host bridges) gives two groups, and a box where every
+    pair sits at the same level gives one."""
+    if count <= 1:
+        return [list(range(count))]
+    levels = [level(i, j) for i in range(count) for j in range(i + 1, count)]
+    top = max(levels)
+    if min(levels) == top:
+        return [list(range(count))]
+    parent = list(range(count))
+
+    def find(x: int) -> int:
+        while parent[x] != x:
+            parent[x] = parent[parent[x]]
+            x = parent[x]
+        return x
+
+    for i in range(count):
+        for j in range(i + 1, count):
+            if level(i, j) < top:
+                parent[find(j)] = find(i)
+    groups: dict[int, list[int]] = {}
+    for i in range(count):
+        groups.setdefault(find(i), []).append(i)
+    return sorted(groups.values())
+
+
+def spread_devices(local_world: int, groups: list[list[int]]) -> list[int]:
+    """GPU ordinal of each local rank: round-robin over the host-link groups, lowest ordinal first,
+    so that N ranks on a box with more GPUs than ranks put equal load on each host attachment.
+    With as many ranks as GPUs every GPU is used and rank r keeps GPU r."""
+    count = sum(len(g) for g in groups)
+    if local_world >= count or len(groups) <= 1:
+        return list(range(local_world))
+    order, queues = [], [list(g) for g in groups]
+    while len(order) < local_world:
+        for q in queues:
+            if q and len(order) < local_world:
+                order.append(q.pop(0))
+    return order
+
+
+def nvml_levels(count: int, nvml=None) -> Callable[[int, int], int] | None:
+    """NVML topology level between the CUDA devices ``i`` and ``j`` of this process (matched by PCI
+    bus id), or None when NVML or the device properties cannot tell."""
+    try:
+        if nvml is None:
+            import pynvml as nvml
+        nvml.nvmlInit()
+        handles = []
+        for i in range(count):
+            p = torch.cuda.get_device_properties(i)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            handles.append(nvml.nvmlDeviceGetHandleByPciBusId(bus))
+        cache = {}
+        for i in range(count):
+            for j in range(i + 1, count):
+                cache[(i, j)] = int(nvml.nvmlDeviceGetTopologyCommonAncestor(handles[i], handles[j]))
+    except Exception:
+        return None
+    return lambda i, j: cache[(min(i, j), max(i, j))]
+
+
+def placed_device(local_rank: int, local_world: int) -> tuple[int, list[list[int]]]:
+    """CUDA device of ``local_rank`` among ``local_world`` ranks on this host, and the host-link
+    groups it was chosen from (one group: identity placement)."""
+    count = torch.cuda.device_count()
+    if local_world >= count:
+        return local_rank, [list(range(count))]
+    level = nvml_levels(count)
+    groups = host_link_groups(count, level) if level is not None else [list(range(count))]
+    return spread_devices(local_world, groups)[local_rank], groups

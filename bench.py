@@ -135,6 +135,9 @@ def parse_args():
     p.add_argument("--shared-pool", action="store_true",
                    help="1 GPU: back the host pool with a shared-memory file registered with the GPU "
                         "(the pool every rank uses on N > 1 GPUs) instead of cudaHostAlloc")
+    p.add_argument("--no-spread", action="store_true",
+                   help="N > 1 with more GPUs visible than ranks: rank r on GPU r instead of spreading the ranks "
+                        "over the host-link groups")
     p.add_argument("--overlap-layers", action="store_true",
                    help="multi-layer resolver workloads (one GPU or --no-balance): layer l+1's LRU step runs on the "
                         "main stream while layer l's swap-in runs on a second stream (an A/B of that pipelining)")
@@ -689,7 +692,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     max_ms, max_e2e_ms = max_over_ranks([sum(step_ms), sum(e2e_ms)], dev)  # slowest rank
     # per rank: its GPU's H2D copy alone and with every rank copying, its timed step and swap-in
     # intervals and the rows installed into its own requests (every rank takes part)
-    by_rank = rows_by_rank([h2d_alone, h2d_peak, sum(step_ms), sum(swapin_ms), installs], dev)
+    by_rank = rows_by_rank([h2d_alone, h2d_peak, sum(step_ms), sum(swapin_ms), installs, local_rank], dev)
     job_stats = reduce_stats(torch.stack([p.stats for p in pools])).cpu().tolist()  # end-of-run (NCCL)
     job_req = cfg.req if cfg.strong else cfg.req * world
     idx_per_step = job_req * cfg.topk * L
@@ -763,9 +766,11 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             "overlap_layers": overlap,
             "step_bracket_ms_p50": statistics.median(bracket_ms),
             "balance": balance_info,
-            "by_rank": [{"h2d_alone_gbs": a, "h2d_concurrent_gbs": c, "step_ms_sum": st, "swapin_ms_sum": sw,
-                         "own_installs": int(n), "own_rows_gbs": n * cfg.row / (sw * 1e-3) / 1e9 if sw > 0 else None}
-                        for a, c, st, sw, n in by_rank],
+            "by_rank": [{"gpu": int(d), "h2d_alone_gbs": a, "h2d_concurrent_gbs": c, "step_ms_sum": st,
+                         "swapin_ms_sum": sw, "own_installs": int(n),
+                         "own_rows_gbs": n * cfg.row / (sw * 1e-3) / 1e9 if sw > 0 else None}
+                        for a, c, st, sw, n, d in by_rank],
+            "placement": PLACEMENT,
             "step_ms_by_rank0": step_ms,
             "verified_rows": verified,
             "cpu_baseline": cpu,
@@ -1502,6 +1507,9 @@ def run_ops(args, world: int, rank: int, local_rank: int):
     print(json.dumps(line), flush=True)
 
 
+PLACEMENT: dict = {"rule": "GPU = local rank"}  # how ranks were placed on this host's GPUs
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1514,6 +1522,14 @@ def main():
         import torch
         import torch.distributed as dist
 
+        from asu_ascend_b200.dist import placed_device
+
+        # With fewer ranks than visible GPUs, spread the ranks over the host-link groups (GPUs that
+        # share a socket or host bridge): rank r then runs on GPU `local_rank` below, not GPU r.
+        local_world = int(os.environ.get("LOCAL_WORLD_SIZE", world))
+        if not args.no_spread:
+            local_rank, groups = placed_device(local_rank, local_world)
+            PLACEMENT.update({"host_link_groups": groups, "rule": "round-robin over host-link groups"})
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     try:

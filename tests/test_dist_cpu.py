@@ -107,3 +107,28 @@ def test_gpu_local_cpus_reads_nvml_affinity_within_the_allowed_set():
             raise RuntimeError("no driver")
 
     assert gpu_local_cpus(0, Broken()) == [] and bind_to_gpu_local_cpus(0, Broken()) == []
+
+
+def test_host_link_groups_and_spread_placement():
+    from asu_ascend_b200.dist import host_link_groups, spread_devices
+
+    # two sockets of four GPUs (NVML levels: 40 within a NUMA node, 50 across the system)
+    two = host_link_groups(8, lambda i, j: 40 if (i < 4) == (j < 4) else 50)
+    assert two == [[0, 1, 2, 3], [4, 5, 6, 7]]
+    assert spread_devices(1, two) == [0]
+    assert spread_devices(2, two) == [0, 4]
+    assert spread_devices(4, two) == [0, 4, 1, 5]
+    assert spread_devices(8, two) == list(range(8))  # as many ranks as GPUs: rank r keeps GPU r
+    # switches below the sockets do not split the groups further: only the widest split counts
+    nested = host_link_groups(8, lambda i, j: 20 if i // 2 == j // 2 else (40 if (i < 4) == (j < 4) else 50))
+    assert nested == two
+    # every pair at the same level: one group, identity placement
+    flat = host_link_groups(8, lambda i, j: 40)
+    assert flat == [list(range(8))] and spread_devices(4, flat) == [0, 1, 2, 3]
+    # uneven groups: round-robin while each group has GPUs left, every GPU at most once
+    uneven = [[0, 1, 2], [3]]
+    assert spread_devices(3, uneven) == [0, 3, 1]
+    for n in range(1, 5):
+        got = spread_devices(n, uneven)
+        assert len(set(got)) == n
+    assert host_link_groups(1, lambda i, j: 0) == [[0]]
