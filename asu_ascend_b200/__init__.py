@@ -14,6 +14,8 @@ if it is not built -- there is no CPU fallback):
 * ``hbm_lookup_update`` mirror of the reference's gather/update extension module
 * ``lru``               per-request exact-LRU slot pools (LruSlotPools)
 * ``host_pool``         pinned mapped host row pool + swap-in gather (HostRowPool)
+* ``dist``              request sharding, end-of-run statistics, rank placement on a host's GPUs
+* ``balance``           swap-in balancing between the ranks of one host (peer stores over NVLink)
 * ``workloads``         seeded synthetic traces (no CUDA needed)
 * ``build``             nvcc build of the library
 """

@@ -74,6 +74,19 @@ def plan_pairs(rates: Sequence[float], req: Sequence[int], min_share: float = 0.
     return pairs
 
 
+def best_plan(measured: Sequence[tuple[float, list[tuple[int, int, int]]]], unbalanced_ms: float | None = None,
+              margin: float = 0.02) -> list[tuple[int, int, int]]:
+    """The measured plan whose slowest rank finished first: ``measured`` holds (slowest rank's
+    swap-in ms, plan) per calibration round (the earlier round wins a tie).  With the unbalanced
+    round's figure, a plan is kept only if it beats it by ``margin``; otherwise every share is 0."""
+    if not measured:
+        return []
+    ms, plan = min(measured, key=lambda x: x[0])
+    if unbalanced_ms is not None and not ms < (1.0 - margin) * unbalanced_ms:
+        return [(o, h, 0) for o, h, _ in plan]
+    return list(plan)
+
+
 def refine_share(req_owner: int, req_helper: int, m: int, owner_ms: float, helper_ms: float) -> int:
     """New share from a round run with share ``m``: the owner swapped in ``req_owner - m`` requests
     in ``owner_ms``, the helper ``req_helper + m`` in ``helper_ms``."""
@@ -288,40 +301,44 @@ class SwapinBalancer:
         """Choose the pairs and shares.  ``run_steps(n)`` runs n steps of the caller's loop (which
         swaps in through ``self.swapin``); every rank must call this with the same arguments.
         ``initial_pairs`` skips the first round (the unbalanced measurement) and starts the
-        refinement from that plan.  Without it, a last round measures the refined plan, which is
-        kept only if the slowest rank's swap-in got at least 2% faster than with no balancing
-        (otherwise every share goes to 0).  Runs at most ``steps * (rounds + 2)`` steps."""
+        refinement from that plan.  Every plan tried is measured, and the one whose slowest rank
+        finished first is kept; without ``initial_pairs`` it must also beat the unbalanced round by
+        2%, else every share goes to 0.  (Shares refined from one round's rates can overshoot: a
+        host link shared by several GPUs serves each faster when the others read less, so the
+        refined plan is not always better than the one it came from.)  Runs at most
+        ``steps * (rounds + 2)`` steps."""
         req = [int(x) for x in self._gather([float(self.R)])[:, 0].tolist()]
+        unbalanced = None
         if initial_pairs is None:
             own, total = self._measure(run_steps, steps)
             g = self._gather([total])
             rates = [req[r] / g[r, 0].item() if g[r, 0] > 0 else 0.0 for r in range(self.world)]
+            unbalanced = max(g[:, 0].tolist())
             self.history.append({"round": 0, "ms": g[:, 0].tolist()})
             self.set_plan(plan_pairs(rates, req, self.min_share))
         else:
             self.set_plan(initial_pairs)
-        for i in range(rounds):
+        measured: list[tuple[float, list[tuple[int, int, int]]]] = []
+        for i in range(rounds + (1 if initial_pairs is None else 0)):
             if not any(m > 0 for _, _, m in self.pairs):
                 break
             own, total = self._measure(run_steps, steps)
             g = self._gather([own, total])
+            measured.append((max(g[:, 1].tolist()), list(self.pairs)))
             self.history.append({"round": i + 1, "own_ms": g[:, 0].tolist(), "ms": g[:, 1].tolist(),
                                  "pairs": [list(p) for p in self.pairs]})
+            if i == rounds:  # the last plan is measured, not refined
+                break
             # a share refined to 0 leaves the pair in place but swaps in locally (no messages)
             self.pairs = [(o, h, refine_share(req[o], req[h], m, g[o, 0].item(), g[h, 1].item()))
                           for o, h, m in self.pairs]
             self._apply_share()
-        if initial_pairs is None and any(m > 0 for _, _, m in self.pairs):
-            # keep the plan only if the slowest rank got faster than with no balancing at all
-            base = max(self.history[0]["ms"])
-            own, total = self._measure(run_steps, steps)
-            g = self._gather([total])
-            kept = max(g[:, 0].tolist()) < 0.98 * base
-            self.history.append({"round": "final", "ms": g[:, 0].tolist(),
-                                 "pairs": [list(p) for p in self.pairs], "kept": kept})
-            if not kept:
-                self.pairs = [(o, h, 0) for o, h, _ in self.pairs]
-                self._apply_share()
+        if self.pairs:
+            self.pairs = best_plan(measured, unbalanced) if measured else [(o, h, 0) for o, h, _ in self.pairs]
+            self._apply_share()
+            self.history.append({"round": "kept", "pairs": [list(p) for p in self.pairs],
+                                 "slowest_ms": min((x[0] for x in measured), default=None),
+                                 "unbalanced_ms": unbalanced})
         return {"pairs": [list(p) for p in self.pairs], "history": self.history}
 
     def _apply_share(self) -> None:

@@ -158,12 +158,110 @@ def nvml_levels(count: int, nvml=None) -> Callable[[int, int], int] | None:
     return lambda i, j: cache[(min(i, j), max(i, j))]
 
 
-def placed_device(local_rank: int, local_world: int) -> tuple[int, list[list[int]]]:
-    """CUDA device of ``local_rank`` among ``local_world`` ranks on this host, and the host-link
-    groups it was chosen from (one group: identity placement)."""
+def placement_candidates(count: int, n: int, groups: list[list[int]] | None = None) -> list[list[int]]:
+    """Device orders worth measuring for ``n`` ranks on ``count`` GPUs: the identity, the GPUs'
+    two halves interleaved (0, count/2, 1, count/2 + 1, ...), and the round-robin over the
+    host-link ``groups`` when NVML shows more than one; first ``n`` entries of each, no repeats."""
+    half = count // 2
+    inter = [d for pair in zip(range(half), range(half, count)) for d in pair] + list(range(2 * half, count))
+    cands = [list(range(n)), inter[:n]]
+    if groups is not None and len(groups) > 1:
+        cands.append(spread_devices(n, groups))
+    out: list[list[int]] = []
+    for c in cands:
+        if c not in out:
+            out.append(c)
+    return out
+
+
+def choose_placement(cands: list[list[int]], rates: list[dict[int, float]], margin: float = 0.05) -> int:
+    """Index of the candidate whose slowest GPU copies fastest with all of them copying at once
+    (``rates[i]``: GB/s per device of candidate i); another candidate replaces the first (the
+    identity) only when its slowest GPU is ``margin`` faster."""
+    slowest = [min(r.values()) if r else 0.0 for r in rates]
+    best = 0
+    for i in range(1, len(cands)):
+        if slowest[i] > slowest[best] * (1.0 + margin):
+            best = i
+    return best
+
+
+def concurrent_h2d_gbs(devices: list[int], nbytes: int = 256 << 20, reps: int = 3) -> dict[int, float]:
+    """Pinned host -> device copy bandwidth of each of ``devices`` with all of them copying at once
+    (one process, one stream per device; median of ``reps``)."""
+    import statistics
+
+    src = {d: torch.empty(nbytes, dtype=torch.uint8).pin_memory() for d in devices}
+    dst = {d: torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{d}") for d in devices}
+    streams = {d: torch.cuda.Stream(device=d) for d in devices}
+    rates: dict[int, list[float]] = {d: [] for d in devices}
+    for _ in range(reps + 1):  # the first round warms up
+        ev = {}
+        for d in devices:
+            torch.cuda.synchronize(d)
+        for d in devices:
+            with torch.cuda.device(d), torch.cuda.stream(streams[d]):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                dst[d].copy_(src[d], non_blocking=True)
+                b.record()
+                ev[d] = (a, b)
+        for d in devices:
+            torch.cuda.synchronize(d)
+        for d in devices:
+            rates[d].append(nbytes / (ev[d][0].elapsed_time(ev[d][1]) * 1e-3) / 1e9)
+    return {d: statistics.median(v[1:]) for d, v in rates.items()}
+
+
+def measure_placement(n: int) -> dict:
+    """Run in a process of its own (it opens a context on every visible GPU): measure each
+    candidate order's concurrent H2D rates and pick one (``choose_placement``)."""
     count = torch.cuda.device_count()
-    if local_world >= count:
-        return local_rank, [list(range(count))]
     level = nvml_levels(count)
-    groups = host_link_groups(count, level) if level is not None else [list(range(count))]
-    return spread_devices(local_world, groups)[local_rank], groups
+    groups = host_link_groups(count, level) if level is not None else None
+    cands = placement_candidates(count, n, groups)
+    rates = [concurrent_h2d_gbs(c) for c in cands]
+    best = choose_placement(cands, rates)
+    return {"devices": cands[best], "candidates": cands,
+            "slowest_gbs": [round(min(r.values()), 1) for r in rates], "host_link_groups": groups}
+
+
+def placed_device(local_rank: int, local_world: int, store=None, key: str = "asu_b200/placement",
+                  timeout_s: float = 180.0) -> tuple[int, dict]:
+    """CUDA device of ``local_rank`` among ``local_world`` ranks on this host, and how it was chosen.
+
+    With as many ranks as visible GPUs, rank r takes GPU r.  With fewer, GPUs can share a host
+    attachment unevenly (on the 8-GPU B200 boxes measured here GPUs 0-3 share ~116 GB/s of host
+    -> device bandwidth while GPUs 4-7 get ~54 GB/s each, and NVML reports every pair at the same
+    topology level), so local rank 0 measures the candidate orders in a child process and puts the
+    choice in ``store`` (a c10d store shared by the host's ranks); the other ranks read it there."""
+    import json
+    import subprocess
+    import sys
+
+    count = torch.cuda.device_count()
+    if local_world >= count or store is None:
+        return local_rank, {"rule": "GPU = local rank"}
+    if local_rank == 0:
+        try:
+            res = subprocess.run([sys.executable, "-m", "asu_ascend_b200.dist", "--measure-placement",
+                                  str(local_world)], capture_output=True, text=True, timeout=timeout_s)
+            info = json.loads(res.stdout.strip().splitlines()[-1]) if res.returncode == 0 else None
+        except (subprocess.TimeoutExpired, ValueError, IndexError):
+            info = None
+        if info is None:
+            info = {"devices": list(range(local_world)), "error": "placement measurement failed"}
+        info["rule"] = "measured: the candidate order whose slowest GPU copies fastest"
+        store.set(key, json.dumps(info))
+    info = json.loads(store.get(key))
+    return int(info["devices"][local_rank]), info
+
+
+if __name__ == "__main__":
+    import json
+    import sys
+
+    if len(sys.argv) == 3 and sys.argv[1] == "--measure-placement":
+        print(json.dumps(measure_placement(int(sys.argv[2]))))
+    else:
+        raise SystemExit("usage: python -m asu_ascend_b200.dist --measure-placement N")

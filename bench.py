@@ -136,8 +136,8 @@ def parse_args():
                    help="1 GPU: back the host pool with a shared-memory file registered with the GPU "
                         "(the pool every rank uses on N > 1 GPUs) instead of cudaHostAlloc")
     p.add_argument("--no-spread", action="store_true",
-                   help="N > 1 with more GPUs visible than ranks: rank r on GPU r instead of spreading the ranks "
-                        "over the host-link groups")
+                   help="N > 1 with more GPUs visible than ranks: rank r on GPU r instead of the measured placement "
+                        "(the GPUs that share the host link least)")
     p.add_argument("--overlap-layers", action="store_true",
                    help="multi-layer resolver workloads (one GPU or --no-balance): layer l+1's LRU step runs on the "
                         "main stream while layer l's swap-in runs on a second stream (an A/B of that pipelining)")
@@ -1524,14 +1524,21 @@ def main():
 
         from asu_ascend_b200.dist import placed_device
 
-        # With fewer ranks than visible GPUs, spread the ranks over the host-link groups (GPUs that
-        # share a socket or host bridge): rank r then runs on GPU `local_rank` below, not GPU r.
+        # The env:// store, opened here so that the ranks can agree on a placement before the process
+        # group binds each of them to a GPU.  With fewer ranks than visible GPUs, local rank 0 measures
+        # which GPUs share the host link least and every rank takes its GPU from that choice: rank r
+        # then runs on GPU `local_rank` below, not GPU r.
+        store, _, _ = next(dist.rendezvous("env://", timeout=timedelta(seconds=300)))
+        store.set_timeout(timedelta(seconds=300))
         local_world = int(os.environ.get("LOCAL_WORLD_SIZE", world))
         if not args.no_spread:
-            local_rank, groups = placed_device(local_rank, local_world)
-            PLACEMENT.update({"host_link_groups": groups, "rule": "round-robin over host-link groups"})
+            local_rank, info = placed_device(local_rank, local_world, store,
+                                             key=f"asu_b200/placement/{os.environ.get('GROUP_RANK', '0')}")
+            PLACEMENT.clear()
+            PLACEMENT.update(info)
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+        dist.init_process_group("nccl", store=store, rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
     try:
         if args.workload in RESOLVER_WORKLOADS:
             run_resolver(args, RESOLVER_WORKLOADS[args.workload], world, rank, local_rank)

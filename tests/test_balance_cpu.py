@@ -14,7 +14,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from asu_ascend_b200.balance import (FdServer, balanced_share, fetch_fd, plan_pairs, refine_share,
+from asu_ascend_b200.balance import (FdServer, balanced_share, best_plan, fetch_fd, plan_pairs, refine_share,
                                      socket_name)
 from asu_ascend_b200.host_pool import SharedRows
 
@@ -55,6 +55,20 @@ def test_refine_share_moves_towards_the_slower_side():
     assert refine_share(128, 128, 20, owner_ms=1.2, helper_ms=1.0) > 20
     assert refine_share(128, 128, 40, owner_ms=0.8, helper_ms=1.2) < 40
     assert refine_share(128, 128, 30, owner_ms=0.0, helper_ms=1.0) == 30
+
+
+def test_best_plan_keeps_the_fastest_measured_round():
+    # the 8-GPU box's calibration: unbalanced 1.73 ms; the first plan 1.31 ms; its refinement
+    # overshot towards 0 (1.62 ms) and the next came back part way (1.53 ms)
+    p1 = [(0, 5, 26), (2, 6, 26), (3, 4, 25), (1, 7, 25)]
+    p2 = [(0, 5, 0), (2, 6, 0), (3, 4, 1), (1, 7, 0)]
+    p3 = [(0, 5, 23), (2, 6, 25), (3, 4, 4), (1, 7, 23)]
+    assert best_plan([(1.306, p1), (1.624, p2), (1.527, p3)], unbalanced_ms=1.731) == p1
+    # no plan beats the unbalanced round by the margin: every share goes to 0, the pairs stay
+    assert best_plan([(1.72, p1)], unbalanced_ms=1.731) == [(o, h, 0) for o, h, _ in p1]
+    # a forced start (no unbalanced round): the fastest measured plan, the earlier one on a tie
+    assert best_plan([(1.0, p1), (1.0, p3)]) == p1
+    assert best_plan([]) == []
 
 
 def test_fd_hand_over_shares_the_pool_pages():

@@ -132,3 +132,61 @@ def test_host_link_groups_and_spread_placement():
         got = spread_devices(n, uneven)
         assert len(set(got)) == n
     assert host_link_groups(1, lambda i, j: 0) == [[0]]
+
+
+def test_placement_candidates_and_choice():
+    from asu_ascend_b200.dist import choose_placement, placement_candidates
+
+    assert placement_candidates(8, 4) == [[0, 1, 2, 3], [0, 4, 1, 5]]
+    assert placement_candidates(8, 1) == [[0]]
+    assert placement_candidates(6, 3) == [[0, 1, 2], [0, 3, 1]]
+    # NVML groups that agree with the halves add nothing new
+    assert placement_candidates(8, 4, [[0, 1, 2, 3], [4, 5, 6, 7]]) == [[0, 1, 2, 3], [0, 4, 1, 5]]
+    cands = placement_candidates(8, 4)
+    # the 8-GPU box: GPUs 0-3 copying together get ~29 GB/s each, GPUs 0, 1, 4, 5 ~54
+    assert choose_placement(cands, [{0: 28.9, 1: 29.0, 2: 28.9, 3: 29.0}, {0: 53.6, 4: 55.3, 1: 53.7, 5: 55.3}]) == 1
+    # within the margin the identity stays
+    assert choose_placement(cands, [{0: 55.0, 1: 55.0}, {0: 55.5, 4: 56.0}]) == 0
+
+
+def test_placed_device_shares_local_rank_0s_choice(monkeypatch):
+    import json
+    import subprocess
+    import threading
+
+    from asu_ascend_b200 import dist as D
+
+    monkeypatch.setattr(torch.cuda, "device_count", lambda: 8)
+    calls = []
+
+    def fake_run(cmd, **kw):
+        calls.append(cmd)
+        out = json.dumps({"devices": [0, 4, 1, 5], "candidates": [[0, 1, 2, 3], [0, 4, 1, 5]],
+                          "slowest_gbs": [28.9, 53.6]})
+        return subprocess.CompletedProcess(cmd, 0, stdout="log line\n" + out + "\n", stderr="")
+
+    monkeypatch.setattr(subprocess, "run", fake_run)
+    store = dist.HashStore()
+    got = {}
+
+    def rank(lr):
+        got[lr] = D.placed_device(lr, 4, store, key="k")
+
+    threads = [threading.Thread(target=rank, args=(lr,)) for lr in (3, 2, 1, 0)]  # readers wait for rank 0
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=30)
+    assert {lr: d for lr, (d, _) in got.items()} == {0: 0, 1: 4, 2: 1, 3: 5}
+    assert len(calls) == 1 and "--measure-placement" in calls[0] and calls[0][-1] == "4"
+    assert got[2][1]["slowest_gbs"] == [28.9, 53.6] and got[2][1]["rule"].startswith("measured")
+    # as many ranks as GPUs, or no store: rank r keeps GPU r and nothing is measured
+    assert D.placed_device(5, 8, store)[0] == 5 and D.placed_device(1, 4, None)[0] == 1
+    assert len(calls) == 1
+
+    # a failed measurement falls back to the identity for every rank
+    monkeypatch.setattr(subprocess, "run", lambda cmd, **kw: subprocess.CompletedProcess(cmd, 1, "", "boom"))
+    store2 = dist.HashStore()
+    assert D.placed_device(0, 4, store2, key="k")[0] == 0
+    d3, info = D.placed_device(3, 4, store2, key="k")
+    assert d3 == 3 and "failed" in info["error"]
