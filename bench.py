@@ -127,11 +127,13 @@ def parse_args():
     p.add_argument("--host-pitch", type=int, default=0,
                    help="bytes between host-pool rows (0: the pool's default, rows up to 1 KiB padded "
                         "to a multiple of 128 bytes)")
-    p.add_argument("--no-balance", action="store_true",
-                   help="resolver workloads on N > 1 GPUs: no swap-in balancing between ranks")
+    p.add_argument("--balance", action="store_true",
+                   help="resolver workloads on N > 1 GPUs: swap-in balancing between ranks (off by default: on the "
+                        "8-GPU box it measured slower than letting every rank swap in its own rows)")
     p.add_argument("--balance-share", type=int, default=0,
-                   help="N > 1: start from a plan in which rank N-1-i swaps in the last M requests of rank i "
-                        "for i < N/2 (skips the unbalanced calibration round; checks the balanced path on any box)")
+                   help="N > 1, implies --balance: start from a plan in which rank N-1-i swaps in the last M requests "
+                        "of rank i for i < N/2 (skips the unbalanced calibration round; checks the balanced path on "
+                        "any box)")
     p.add_argument("--shared-pool", action="store_true",
                    help="1 GPU: back the host pool with a shared-memory file registered with the GPU "
                         "(the pool every rank uses on N > 1 GPUs) instead of cudaHostAlloc")
@@ -139,7 +141,7 @@ def parse_args():
                    help="N > 1 with more GPUs visible than ranks: rank r on GPU r instead of the measured placement "
                         "(the GPUs that share the host link least)")
     p.add_argument("--overlap-layers", action="store_true",
-                   help="multi-layer resolver workloads (one GPU or --no-balance): layer l+1's LRU step runs on the "
+                   help="multi-layer resolver workloads (without --balance): layer l+1's LRU step runs on the "
                         "main stream while layer l's swap-in runs on a second stream (an A/B of that pipelining)")
     p.add_argument("--verify", action="store_true",
                    help="resolver workloads: after the run, check every resident slot row of every "
@@ -480,7 +482,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     else:
         r0, R = rank * cfg.req, cfg.req
     K_steps, W, L = args.steps, args.warmup, cfg.layers
-    balance = world > 1 and not args.no_balance
+    balance = world > 1 and (args.balance or args.balance_share > 0)
     cal = 0 if not balance else CAL_STEPS * (CAL_ROUNDS + (0 if args.balance_share else 2))
     base = args.prefill + cal + W
     cpu_leg = world == 1 and not args.no_cpu_baseline and cfg.name == "resolver"
@@ -524,7 +526,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     # layer l's swap-in (and its output copy) to finish reading them.
     overlap = args.overlap_layers and L > 1
     if args.overlap_layers and bal is not None:
-        raise SystemExit("--overlap-layers runs the swap-ins locally: use it on one GPU or with --no-balance")
+        raise SystemExit("--overlap-layers runs the swap-ins locally: use it without --balance")
     main = torch.cuda.current_stream(dev)
     side = torch.cuda.Stream(dev) if overlap else None
 
@@ -735,15 +737,17 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             # dominant kernel by time (ncu launch list: ~98% of the resolver step), bound by the host link
             "roofline": {"bound": "host_link",
                          "kernel": "swapin_bulk_kernel" if cfg.row <= 1024 else "swapin_kernel",
-                         "achieved": swap_gbs, "peak": h2d_peak, "unit": "GB/s", "frac": swap_gbs / h2d_peak,
+                         "achieved": swap_gbs, "peak": h2d_alone, "unit": "GB/s", "frac": swap_gbs / h2d_alone,
                          "traffic": (SWAPIN_PCIE_READ_BYTES_PER_LAUNCH * installs / launches / SWAPIN_NCU_INSTALLS
                                      if cfg.row == 656 and host.pitch == 768 else None),
                          "traffic_kind": "PCIe read bytes per launch (ncu pcie__read_bytes of the resolver "
                                          "workload, scaled to this run's installs per launch)",
                          "traffic_source": SWAPIN_TRAFFIC_SOURCE,
-                         "peak_source": ("pinned cudaMemcpyAsync H2D 256 MiB, best of 10, this run"
-                                         + ("" if world == 1 else ", all ranks copying at once")),
-                         "peak_alone": h2d_alone},
+                         # rank 0's GPU copying alone; with N > 1 the ranks share the host, so the
+                         # fraction also shows that contention (the copy engines' figure with all
+                         # ranks copying at once is beside it: SM reads of mapped memory exceed it)
+                         "peak_source": "pinned cudaMemcpyAsync H2D 256 MiB, best of 10, this run, this GPU alone",
+                         "peak_concurrent_copy": h2d_peak if world > 1 else None},
             "roofline_lru": {"bound": "hbm", "kernel": "lru_step_kernel", "achieved": achieved, "peak": hbm_peak,
                              "unit": "GB/s", "frac": achieved / hbm_peak,
                              "traffic": LRU_DRAM_BYTES_PER_LAUNCH if cfg.name == "resolver" else None,
