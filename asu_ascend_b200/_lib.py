@@ -70,6 +70,7 @@ _SIGS = {
     "asu_host_pool_writeback": [_P, _P, c_int64, c_uint32, c_uint32, _P, c_int64, c_uint64, _P, _P, c_int64, _P],
     "asu_host_pool_free": [_P],
     "asu_host_device_pointer": [_P, POINTER(c_void_p)],
+    "asu_mapped_copy": [_P, _P, _P, c_uint64],
     "asu_selftest_bounded_wait": [_P, c_int32, _P],
     "asu_kv_resolver_do": [_P, _P, c_int64, _P, _P, _P, _P, _P, _P, c_int64, _P, c_int64, _P, _P, _P, _P, c_int64,
                            c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, _P, _P, _P],

@@ -228,3 +228,38 @@ class HostRowPool:
 
 def check_status(status: torch.Tensor, what: str, ignore: int = 0) -> None:
     raise_on_status(status, what, ignore)
+
+
+def _device_address(t: torch.Tensor, dev: torch.device, name: str) -> int:
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+    if t.device.type == "cuda":
+        if t.device != dev:
+            raise RuntimeError(f"{name} must be on {dev}")
+        return t.data_ptr()
+    if not t.is_pinned():
+        raise RuntimeError(f"{name} must be a CUDA tensor or pinned host memory")
+    d = ctypes.c_void_p()
+    check(lib.asu_host_device_pointer(t.data_ptr(), ctypes.byref(d)), f"{name}: device address of pinned memory")
+    return d.value
+
+
+def mapped_copy_(dst: torch.Tensor, src: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """``dst.copy_(src)`` of equal-size contiguous tensors, one in HBM and the other in pinned host
+    memory (or both in HBM), done by the SMs through the host mapping instead of a copy engine
+    (``asu_mapped_copy``): for per-step uploads and read-backs on a box whose copy engines share
+    the host unevenly.  Bytes are copied as they are (no dtype conversion).  Asynchronous on
+    ``stream`` (default: the current stream of the CUDA side); synchronise before reading a host
+    result."""
+    if dst.numel() * dst.element_size() != src.numel() * src.element_size():
+        raise RuntimeError("mapped_copy_: dst and src must have the same size in bytes")
+    cuda_side = dst if dst.device.type == "cuda" else src
+    if cuda_side.device.type != "cuda":
+        raise RuntimeError("mapped_copy_: one of dst and src must be a CUDA tensor")
+    dev = cuda_side.device
+    d = _device_address(dst, dev, "dst")
+    s = _device_address(src, dev, "src")
+    st = (stream or torch.cuda.current_stream(dev)).cuda_stream
+    with torch.cuda.device(dev):
+        check(lib.asu_mapped_copy(st, d, s, dst.numel() * dst.element_size()), "asu_mapped_copy")
+    return dst

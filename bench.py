@@ -470,7 +470,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
 
     asu_ascend_b200.load()
     from asu_ascend_b200.dist import bind_to_gpu_local_cpus, max_over_ranks, reduce_stats, rows_by_rank, shard_range
-    from asu_ascend_b200.host_pool import HostRowPool, check_status
+    from asu_ascend_b200.host_pool import HostRowPool, check_status, mapped_copy_
     from asu_ascend_b200.lru import LruSlotPools
     from asu_ascend_b200.workloads import record_addresses_torch
 
@@ -651,8 +651,10 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     hit_host = torch.empty((R, cfg.topk), dtype=torch.bool, pin_memory=True)
     q_ins = [torch.empty((R, cfg.topk), dtype=torch.int32, device=dev) for _ in range(2 if overlap else 1)]
     ev2 = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K_steps)]
-    # The slot ids and hit mask go back on a second stream while the swap-in reads host rows:
-    # the two copies run in opposite directions of the host link.
+    # The top-k goes up and the slot ids and hit mask come back through the host mapping, copied by
+    # the SMs (asu_mapped_copy): with several GPUs on one host the copy engines get the smallest share
+    # of it.  The read-back runs on a second stream while the swap-in reads host rows: the two run in
+    # opposite directions of the host link.
     copy_stream = torch.cuda.Stream(dev)
     rank_sync(torch)
     for k in range(K_steps):
@@ -663,12 +665,12 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             o = outs[(k * L + layer) % 2]
             q_in = q_ins[layer % len(q_ins)]
             pipe.before_step(layer)
-            q_in.copy_(q_host[base2 + k, layer], non_blocking=True)
+            mapped_copy_(q_in, q_host[base2 + k, layer])  # SM reads of the pinned top-k
             pools[layer].step(q_in, out=o)
             copy_stream.wait_stream(main)
             with torch.cuda.stream(copy_stream):
-                slot_host.copy_(o.slot, non_blocking=True)
-                hit_host.copy_(o.hit, non_blocking=True)
+                mapped_copy_(slot_host, o.slot)  # SM writes into pinned host memory
+                mapped_copy_(hit_host, o.hit)
             if overlap:
                 copied = torch.cuda.Event()
                 copied.record(copy_stream)
@@ -763,6 +765,8 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             "e2e": {"value": idx_per_step * K_steps / (max_e2e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": R * cfg.topk * 4 * L, "d2h_bytes_per_step": R * cfg.topk * 5 * L},
             "gpu_launches": 2 * launches,
+            # the e2e region adds the top-k upload and the two read-backs (asu_mapped_copy) per layer
+            "gpu_launches_e2e": 5 * launches,
             "job_stats": dict(zip(LruSlotPools.STAT_NAMES, job_stats)),
             "host_cpus_bound": len(bound_cpus),
             "note_step_time": ("the step's event bracket (layers pipelined over two streams)" if overlap else

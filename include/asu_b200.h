@@ -214,6 +214,15 @@ int asu_host_pool_free(void* host_ptr);
  * Used to let kernels read their inputs from and write their outputs to host buffers directly. */
 int asu_host_device_pointer(const void* host_ptr, void** device_ptr);
 
+/* No reference counterpart (the reference's top-k and resolved slots stay on the NPU).  Copies
+ * `bytes` from src to dst with the SMs, where one side is HBM and the other page-locked, mapped
+ * host memory given by its device address (asu_host_device_pointer), or both are HBM: a host
+ * <-> device transfer that does not use a copy engine, for a caller's small per-step uploads and
+ * read-backs on a box whose copy engines share the host unevenly.  16-, 4- or 1-byte units by the
+ * alignment of both pointers and the size; the ranges must not overlap (ASU_ERR_ARG).
+ * Asynchronous on `stream`, a programmatic dependent launch. */
+int asu_mapped_copy(void* stream, void* dst, const void* src, uint64_t bytes);
+
 /* Self-test of the bounded device wait that asu_swapin_gather's TMA copies use (no reference
  * counterpart).  One thread waits on an mbarrier with an arrival count of one: arrive == 0 gives
  * a barrier nothing arrives at, so the wait runs out and ASU_ST_TIMEOUT is OR-ed
