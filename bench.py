@@ -696,7 +696,8 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     max_ms, max_e2e_ms = max_over_ranks([sum(step_ms), sum(e2e_ms)], dev)  # slowest rank
     # per rank: its GPU's H2D copy alone and with every rank copying, its timed step and swap-in
     # intervals and the rows installed into its own requests (every rank takes part)
-    by_rank = rows_by_rank([h2d_alone, h2d_peak, sum(step_ms), sum(swapin_ms), installs, local_rank], dev)
+    by_rank = rows_by_rank([h2d_alone, h2d_peak, sum(step_ms), sum(swapin_ms), installs, local_rank, sum(e2e_ms)],
+                           dev)
     job_stats = reduce_stats(torch.stack([p.stats for p in pools])).cpu().tolist()  # end-of-run (NCCL)
     job_req = cfg.req if cfg.strong else cfg.req * world
     idx_per_step = job_req * cfg.topk * L
@@ -775,11 +776,12 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             "step_bracket_ms_p50": statistics.median(bracket_ms),
             "balance": balance_info,
             "by_rank": [{"gpu": int(d), "h2d_alone_gbs": a, "h2d_concurrent_gbs": c, "step_ms_sum": st,
-                         "swapin_ms_sum": sw, "own_installs": int(n),
+                         "swapin_ms_sum": sw, "e2e_ms_sum": e, "own_installs": int(n),
                          "own_rows_gbs": n * cfg.row / (sw * 1e-3) / 1e9 if sw > 0 else None}
-                        for a, c, st, sw, n, d in by_rank],
+                        for a, c, st, sw, n, d, e in by_rank],
             "placement": PLACEMENT,
             "step_ms_by_rank0": step_ms,
+            "e2e_ms_by_rank0": e2e_ms,
             "verified_rows": verified,
             "cpu_baseline": cpu,
             "clocks": clk,
