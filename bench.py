@@ -616,9 +616,11 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
                 a.record()
                 pools[layer].step(q, out=o)
                 b.record()
+                pipe.swapin(layer, q, o, after=b, end_event=c)
+                # bookkeeping after the intervals (on the main stream, which the swap-in leaves
+                # free when the layers are pipelined)
                 free_after[k * L + layer] = pools[layer].free_count.sum()
                 evicting[k * L + layer] = (o.evicted_count > 0).sum()
-                pipe.swapin(layer, q, o, after=b, end_event=c)
             pipe.end_step()
             brackets[k][1].record()
 
