@@ -486,7 +486,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     cal = 0 if not balance else CAL_STEPS * (CAL_ROUNDS + (0 if args.balance_share else 2))
     base = args.prefill + cal + W
     cpu_leg = world == 1 and not args.no_cpu_baseline and cfg.name == "resolver"
-    n_steps = base + (max(2 * K_steps, CPU_CYCLE_STEPS) if cpu_leg else 2 * K_steps)
+    n_steps = base + (max(2 * K_steps + W, CPU_CYCLE_STEPS) if cpu_leg else 2 * K_steps + W)
     trace = make_trace(cfg, R, trace_seed(args, r0), n_steps)
     q_dev = torch.from_numpy(trace).to(dev)
     q_host = torch.from_numpy(trace).pin_memory()
@@ -653,36 +653,42 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     hit_host = torch.empty((R, cfg.topk), dtype=torch.bool, pin_memory=True)
     q_ins = [torch.empty((R, cfg.topk), dtype=torch.int32, device=dev) for _ in range(2 if overlap else 1)]
     ev2 = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K_steps)]
+    ev2_warm = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(W)]
     # The top-k goes up and the slot ids and hit mask come back through the host mapping, copied by
     # the SMs (asu_mapped_copy): with several GPUs on one host the copy engines get the smallest share
     # of it.  The read-back runs on a second stream while the swap-in reads host rows: the two run in
     # opposite directions of the host link.
     copy_stream = torch.cuda.Stream(dev)
+
+    def e2e_steps(first, events):
+        for k, (e0, e1) in enumerate(events):
+            flush()
+            torch.cuda._sleep(spin)
+            e0.record()
+            for layer in range(L):
+                o = outs[(k * L + layer) % 2]
+                q_in = q_ins[layer % len(q_ins)]
+                pipe.before_step(layer)
+                mapped_copy_(q_in, q_host[first + k, layer])  # SM reads of the pinned top-k
+                pools[layer].step(q_in, out=o)
+                copy_stream.wait_stream(main)
+                with torch.cuda.stream(copy_stream):
+                    mapped_copy_(slot_host, o.slot)  # SM writes into pinned host memory
+                    mapped_copy_(hit_host, o.hit)
+                if overlap:
+                    copied = torch.cuda.Event()
+                    copied.record(copy_stream)
+                    pipe.swapin(layer, q_in, o, copy_done=copied)
+                else:
+                    swapin(layer, q_in, o)
+                    main.wait_stream(copy_stream)  # the outputs' buffer is reused two layers later
+            pipe.end_step()
+            main.wait_stream(copy_stream)
+            e1.record()
+
+    e2e_steps(base2, ev2_warm)  # untimed warm-up of the e2e loop's own code (first uses happen here)
     rank_sync(torch)
-    for k in range(K_steps):
-        flush()
-        torch.cuda._sleep(spin)
-        ev2[k][0].record()
-        for layer in range(L):
-            o = outs[(k * L + layer) % 2]
-            q_in = q_ins[layer % len(q_ins)]
-            pipe.before_step(layer)
-            mapped_copy_(q_in, q_host[base2 + k, layer])  # SM reads of the pinned top-k
-            pools[layer].step(q_in, out=o)
-            copy_stream.wait_stream(main)
-            with torch.cuda.stream(copy_stream):
-                mapped_copy_(slot_host, o.slot)  # SM writes into pinned host memory
-                mapped_copy_(hit_host, o.hit)
-            if overlap:
-                copied = torch.cuda.Event()
-                copied.record(copy_stream)
-                pipe.swapin(layer, q_in, o, copy_done=copied)
-            else:
-                swapin(layer, q_in, o)
-                main.wait_stream(copy_stream)  # the outputs' buffer is reused two layers later
-        pipe.end_step()
-        main.wait_stream(copy_stream)
-        ev2[k][1].record()
+    e2e_steps(base2 + W, ev2)
     rank_sync(torch)
     e2e_ms = [e[0].elapsed_time(e[1]) for e in ev2]
     floor_us = event_floor_us(torch, flush, spin, K_steps)
@@ -1032,9 +1038,9 @@ def run_decode(args, world: int, rank: int, local_rank: int):
     torch.cuda.set_device(dev)
     L, bs, K = args.layers, DECODE_BLOCK, args.steps
     base = args.prefill + args.warmup
-    n_steps = base + 2 * K
+    n_steps = base + 2 * K + args.warmup
     if n_steps > 4096:
-        raise SystemExit("decode workload: prefill + warmup + 2 x steps must stay below 4096")
+        raise SystemExit("decode workload: prefill + 2 x (warmup + steps) must stay below 4096")
     actual0 = DECODE_MAX_SEQ - n_steps - 28
     prefix = (actual0 // bs) * bs
     nblk = DECODE_MAX_SEQ // bs
@@ -1125,7 +1131,7 @@ def run_decode(args, world: int, rank: int, local_rank: int):
     rank_sync(torch)
     free_mid = torch.stack([c.free_slot_count for c in ctxs]).sum().item()
     stats_timed = (mgr._banks[0].lru_stats.sum(0) - stats_before).cpu().tolist() if lru else None
-    for k in range(K):
+    for k in range(args.warmup + K):  # the first `warmup` steps warm the e2e loop up, untimed
         flush()
         torch.cuda.synchronize()
         a.record()
@@ -1135,7 +1141,8 @@ def run_decode(args, world: int, rank: int, local_rank: int):
         out_host.copy_(out_dev, non_blocking=True)
         b.record()
         b.synchronize()
-        ms_e2e.append(a.elapsed_time(b))
+        if k >= args.warmup:
+            ms_e2e.append(a.elapsed_time(b))
         advance()
     rank_sync(torch)
     clock_info = clocks.stop()
