@@ -654,22 +654,29 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     q_ins = [torch.empty((R, cfg.topk), dtype=torch.int32, device=dev) for _ in range(2 if overlap else 1)]
     ev2 = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K_steps)]
     ev2_warm = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(W)]
+    # per step and layer: the top-k upload's own interval; per step: the host time to queue the step
+    up_ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(L)] for _ in range(K_steps)]
+    up_warm = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(L)] for _ in range(W)]
+    host_ms: list[float] = []
     # The top-k goes up and the slot ids and hit mask come back through the host mapping, copied by
     # the SMs (asu_mapped_copy): with several GPUs on one host the copy engines get the smallest share
     # of it.  The read-back runs on a second stream while the swap-in reads host rows: the two run in
     # opposite directions of the host link.
     copy_stream = torch.cuda.Stream(dev)
 
-    def e2e_steps(first, events):
+    def e2e_steps(first, events, uploads, host=None):
         for k, (e0, e1) in enumerate(events):
             flush()
             torch.cuda._sleep(spin)
+            t0 = time.perf_counter()
             e0.record()
             for layer in range(L):
                 o = outs[(k * L + layer) % 2]
                 q_in = q_ins[layer % len(q_ins)]
                 pipe.before_step(layer)
+                uploads[k][layer][0].record()
                 mapped_copy_(q_in, q_host[first + k, layer])  # SM reads of the pinned top-k
+                uploads[k][layer][1].record()
                 pools[layer].step(q_in, out=o)
                 copy_stream.wait_stream(main)
                 with torch.cuda.stream(copy_stream):
@@ -685,11 +692,14 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             pipe.end_step()
             main.wait_stream(copy_stream)
             e1.record()
+            if host is not None:
+                host.append((time.perf_counter() - t0) * 1e3)
 
-    e2e_steps(base2, ev2_warm)  # untimed warm-up of the e2e loop's own code (first uses happen here)
+    e2e_steps(base2, ev2_warm, up_warm)  # untimed warm-up of the e2e loop's own code (first uses happen here)
     rank_sync(torch)
-    e2e_steps(base2 + W, ev2)
+    e2e_steps(base2 + W, ev2, up_ev, host_ms)
     rank_sync(torch)
+    upload_ms = [sum(a.elapsed_time(b) for a, b in step) for step in up_ev]
     e2e_ms = [e[0].elapsed_time(e[1]) for e in ev2]
     floor_us = event_floor_us(torch, flush, spin, K_steps)
     for p in pools:
@@ -704,8 +714,8 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     max_ms, max_e2e_ms = max_over_ranks([sum(step_ms), sum(e2e_ms)], dev)  # slowest rank
     # per rank: its GPU's H2D copy alone and with every rank copying, its timed step and swap-in
     # intervals and the rows installed into its own requests (every rank takes part)
-    by_rank = rows_by_rank([h2d_alone, h2d_peak, sum(step_ms), sum(swapin_ms), installs, local_rank, sum(e2e_ms)],
-                           dev)
+    by_rank = rows_by_rank([h2d_alone, h2d_peak, sum(step_ms), sum(swapin_ms), installs, local_rank, sum(e2e_ms),
+                            sum(upload_ms), statistics.median(host_ms)], dev)
     job_stats = reduce_stats(torch.stack([p.stats for p in pools])).cpu().tolist()  # end-of-run (NCCL)
     job_req = cfg.req if cfg.strong else cfg.req * world
     idx_per_step = job_req * cfg.topk * L
@@ -784,9 +794,9 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             "step_bracket_ms_p50": statistics.median(bracket_ms),
             "balance": balance_info,
             "by_rank": [{"gpu": int(d), "h2d_alone_gbs": a, "h2d_concurrent_gbs": c, "step_ms_sum": st,
-                         "swapin_ms_sum": sw, "e2e_ms_sum": e, "own_installs": int(n),
-                         "own_rows_gbs": n * cfg.row / (sw * 1e-3) / 1e9 if sw > 0 else None}
-                        for a, c, st, sw, n, d, e in by_rank],
+                         "swapin_ms_sum": sw, "e2e_ms_sum": e, "e2e_upload_ms_sum": up, "e2e_host_ms_p50": hm,
+                         "own_installs": int(n), "own_rows_gbs": n * cfg.row / (sw * 1e-3) / 1e9 if sw > 0 else None}
+                        for a, c, st, sw, n, d, e, up, hm in by_rank],
             "placement": PLACEMENT,
             "step_ms_by_rank0": step_ms,
             "e2e_ms_by_rank0": e2e_ms,
