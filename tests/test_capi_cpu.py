@@ -79,6 +79,21 @@ def test_argument_validation_rejects_before_launch(lib):
     assert L.asu_kv_resolver_do(None, 1, 4, 1, 1, 1, 1, 1, 1, 4, 1, 1, 1, 1, 1, 1, 4, 4, 4, 4, 4, 4, 0, 1, 1,
                                 None) == lib.ASU_ERR_ARG
     assert L.asu_kv_resolver_workspace_bytes(2048) == ((1 + 4096) * 4 + 15) // 16 * 16
+    # SM-driven host copy: nothing to copy, null pointers, overlapping ranges
+    assert L.asu_mapped_copy(None, None, None, 0) == lib.ASU_OK
+    assert L.asu_mapped_copy(None, None, 4096, 16) == lib.ASU_ERR_ARG
+    assert L.asu_mapped_copy(None, 4096, 4096 + 8, 16) == lib.ASU_ERR_ARG
+
+
+def test_mapped_copy_wrapper_checks_its_arguments_on_the_host():
+    import torch
+
+    from asu_ascend_b200.host_pool import mapped_copy_
+
+    with pytest.raises(RuntimeError, match="same size"):
+        mapped_copy_(torch.zeros(4, dtype=torch.uint8), torch.zeros(8, dtype=torch.uint8))
+    with pytest.raises(RuntimeError, match="CUDA tensor"):
+        mapped_copy_(torch.zeros(4), torch.zeros(4))
 
 
 def test_torch_ops_carry_reference_schemas():
