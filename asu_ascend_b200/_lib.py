@@ -57,6 +57,8 @@ _SIGS = {
     "asu_hbm_index_lookup_simt_ex": [_P, _P, _P, _P, _P, _P, _P, c_uint32, c_uint32, c_uint32, c_uint32, _P],
     "asu_lru_step": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, c_uint32, _P, _P, _P, c_uint32, c_uint32, c_uint32,
                      c_uint32, c_uint32],
+    "asu_lru_step_host_query": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, c_uint32, _P, _P, _P, c_uint32,
+                                c_uint32, c_uint32, c_uint32, c_uint32],
     "asu_swapin_gather": [_P, _P, c_int64, c_uint32, c_uint32, _P, c_uint32, _P, _P, _P, c_uint32, _P, c_uint32,
                           c_uint32, _P],
     "asu_swapin_gather_to_peer": [_P, _P, c_int64, c_uint32, c_uint32, _P, c_uint32, _P, _P, _P, c_uint32, _P,

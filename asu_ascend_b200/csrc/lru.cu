@@ -46,14 +46,17 @@ __device__ __forceinline__ uint32_t hash_slot(int32_t key, int log2h) {
     return (static_cast<uint32_t>(key) * 0x9E3779B1u) >> (32 - log2h);
 }
 
-template <int IPT_Q, int IPT_S>
+// kCopyQuery: `query` may be pinned, mapped host memory (read over the host link, so a host caller
+// needs no upload of its own), and every query is also stored to query_copy [R, Q] in HBM for the
+// swap-in that follows.
+template <int IPT_Q, int IPT_S, bool kCopyQuery>
 __global__ void __launch_bounds__(kThreads)
 lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* __restrict__ order,
                 int32_t* __restrict__ stack, int32_t* __restrict__ count, const int32_t* __restrict__ query,
-                int32_t* __restrict__ slot_out, uint8_t* __restrict__ hit_mask, uint8_t* __restrict__ install_mask,
-                int32_t* __restrict__ evicted, uint32_t ev_stride, int32_t* __restrict__ ev_count,
-                int64_t* __restrict__ stats, int32_t* status, uint32_t req_num, uint32_t K, uint32_t S, uint32_t Q,
-                uint32_t target, int log2h) {
+                int32_t* __restrict__ query_copy, int32_t* __restrict__ slot_out, uint8_t* __restrict__ hit_mask,
+                uint8_t* __restrict__ install_mask, int32_t* __restrict__ evicted, uint32_t ev_stride,
+                int32_t* __restrict__ ev_count, int64_t* __restrict__ stats, int32_t* status, uint32_t req_num,
+                uint32_t K, uint32_t S, uint32_t Q, uint32_t target, int log2h) {
     pdl_wait();     // launched with launch_pdl: stream order for every access below
     pdl_trigger();  // the swap-in that consumes this step may be scheduled now
     extern __shared__ int32_t smem[];
@@ -108,6 +111,13 @@ lru_step_kernel(int32_t* __restrict__ t2s, int32_t* __restrict__ s2t, int32_t* _
             if (pos < Q) {
                 key[j] = __ldg(qrow + pos);
                 if (static_cast<uint32_t>(key[j]) < K) g[j] = ld_cg(trow + key[j]);
+            }
+        }
+        if constexpr (kCopyQuery) {
+#pragma unroll
+            for (int j = 0; j < IPT_Q; ++j) {
+                const uint32_t pos = tid * IPT_Q + j;
+                if (pos < Q) query_copy[static_cast<uint64_t>(r) * Q + pos] = key[j];
             }
         }
         {
@@ -429,32 +439,33 @@ inline size_t lru_smem_bytes(uint32_t S, uint32_t Q, int* log2h_out) {
     return bytes;
 }
 
-template <int IPT_Q, int IPT_S>
+template <int IPT_Q, int IPT_S, bool kCopyQuery>
 int launch_lru(cudaStream_t s, int32_t* t2s, int32_t* s2t, int32_t* order, int32_t* stack, int32_t* count,
-               const int32_t* query, int32_t* slot_out, uint8_t* hit, uint8_t* inst, int32_t* evicted,
-               uint32_t ev_stride, int32_t* ev_count, int64_t* stats, int32_t* status, uint32_t R, uint32_t K,
-               uint32_t S, uint32_t Q, uint32_t target) {
+               const int32_t* query, int32_t* query_copy, int32_t* slot_out, uint8_t* hit, uint8_t* inst,
+               int32_t* evicted, uint32_t ev_stride, int32_t* ev_count, int64_t* stats, int32_t* status, uint32_t R,
+               uint32_t K, uint32_t S, uint32_t Q, uint32_t target) {
     int log2h = 0;
     const size_t smem = lru_smem_bytes(S, Q, &log2h);
     int max_dynamic = 0;
-    const int rc = asu_max_dynamic_smem(reinterpret_cast<const void*>(lru_step_kernel<IPT_Q, IPT_S>), &max_dynamic);
+    const int rc = asu_max_dynamic_smem(reinterpret_cast<const void*>(lru_step_kernel<IPT_Q, IPT_S, kCopyQuery>),
+                                        &max_dynamic);
     if (rc != ASU_OK) return rc;
     if (smem > static_cast<size_t>(max_dynamic)) return ASU_ERR_ARG;
     const uint32_t grid = R < 65535u ? R : 65535u;
-    return launch_pdl(lru_step_kernel<IPT_Q, IPT_S>, dim3(grid), dim3(kThreads), smem, s, t2s, s2t, order, stack,
-                      count, query, slot_out, hit, inst, evicted, ev_stride, ev_count, stats, status, R, K, S, Q,
-                      target, log2h);
+    return launch_pdl(lru_step_kernel<IPT_Q, IPT_S, kCopyQuery>, dim3(grid), dim3(kThreads), smem, s, t2s, s2t,
+                      order, stack, count, query, query_copy, slot_out, hit, inst, evicted, ev_stride, ev_count, stats,
+                      status, R, K, S, Q, target, log2h);
 }
 
-template <int IPT_Q>
+template <int IPT_Q, bool kCopyQuery>
 int dispatch_s(uint32_t S, cudaStream_t s, int32_t* t2s, int32_t* s2t, int32_t* order, int32_t* stack,
-               int32_t* count, const int32_t* query, int32_t* slot_out, uint8_t* hit, uint8_t* inst,
-               int32_t* evicted, uint32_t ev_stride, int32_t* ev_count, int64_t* stats, int32_t* status, uint32_t R,
-               uint32_t K, uint32_t Q, uint32_t target) {
+               int32_t* count, const int32_t* query, int32_t* query_copy, int32_t* slot_out, uint8_t* hit,
+               uint8_t* inst, int32_t* evicted, uint32_t ev_stride, int32_t* ev_count, int64_t* stats, int32_t* status,
+               uint32_t R, uint32_t K, uint32_t Q, uint32_t target) {
 #define ASU_LRU_CASE(N)                                                                                           \
     if (S <= static_cast<uint32_t>(kThreads * N))                                                                 \
-        return launch_lru<IPT_Q, N>(s, t2s, s2t, order, stack, count, query, slot_out, hit, inst, evicted, ev_stride, \
-                                    ev_count, stats, status, R, K, S, Q, target);
+        return launch_lru<IPT_Q, N, kCopyQuery>(s, t2s, s2t, order, stack, count, query, query_copy, slot_out, hit,   \
+                                                inst, evicted, ev_stride, ev_count, stats, status, R, K, S, Q, target);
     ASU_LRU_CASE(2)
     ASU_LRU_CASE(4)
     ASU_LRU_CASE(8)
@@ -468,14 +479,18 @@ int dispatch_s(uint32_t S, cudaStream_t s, int32_t* t2s, int32_t* s2t, int32_t* 
 
 using namespace asu;
 
-extern "C" int asu_lru_step(void* stream, int32_t* token_to_slot, int32_t* slot_to_token, int32_t* lru_order,
-                            int32_t* free_stack, int32_t* free_count, const int32_t* query, int32_t* slot_out,
-                            uint8_t* hit_mask, uint8_t* install_mask, int32_t* evicted, uint32_t evicted_stride,
-                            int32_t* evicted_count, int64_t* stats, int32_t* status, uint32_t req_num,
-                            uint32_t key_space, uint32_t slot_count, uint32_t query_count, uint32_t free_target) {
+namespace {
+
+template <bool kCopyQuery>
+int lru_step(void* stream, int32_t* token_to_slot, int32_t* slot_to_token, int32_t* lru_order, int32_t* free_stack,
+             int32_t* free_count, const int32_t* query, int32_t* query_copy, int32_t* slot_out, uint8_t* hit_mask,
+             uint8_t* install_mask, int32_t* evicted, uint32_t evicted_stride, int32_t* evicted_count, int64_t* stats,
+             int32_t* status, uint32_t req_num, uint32_t key_space, uint32_t slot_count, uint32_t query_count,
+             uint32_t free_target) {
     if (req_num == 0) return ASU_OK;
     if (!token_to_slot || !slot_to_token || !lru_order || !free_stack || !free_count || !evicted_count ||
-        (query_count && (!query || !slot_out || !hit_mask || !install_mask)))
+        (query_count && (!query || !slot_out || !hit_mask || !install_mask)) ||
+        (kCopyQuery && query_count && !query_copy))
         return ASU_ERR_ARG;
     if (key_space == 0 || key_space > 0x7fffffffu || slot_count == 0 || slot_count > 16384u ||
         query_count > 4096u)
@@ -484,10 +499,35 @@ extern "C" int asu_lru_step(void* stream, int32_t* token_to_slot, int32_t* slot_
     if (tgt > 0 && (evicted == nullptr || evicted_stride < tgt)) return ASU_ERR_ARG;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (query_count <= 2048u)
-        return dispatch_s<2>(slot_count, s, token_to_slot, slot_to_token, lru_order, free_stack, free_count, query,
-                             slot_out, hit_mask, install_mask, evicted, evicted_stride, evicted_count, stats, status,
-                             req_num, key_space, query_count, free_target);
-    return dispatch_s<4>(slot_count, s, token_to_slot, slot_to_token, lru_order, free_stack, free_count, query,
-                         slot_out, hit_mask, install_mask, evicted, evicted_stride, evicted_count, stats, status,
-                         req_num, key_space, query_count, free_target);
+        return dispatch_s<2, kCopyQuery>(slot_count, s, token_to_slot, slot_to_token, lru_order, free_stack,
+                                         free_count, query, query_copy, slot_out, hit_mask, install_mask, evicted,
+                                         evicted_stride, evicted_count, stats, status, req_num, key_space,
+                                         query_count, free_target);
+    return dispatch_s<4, kCopyQuery>(slot_count, s, token_to_slot, slot_to_token, lru_order, free_stack, free_count,
+                                     query, query_copy, slot_out, hit_mask, install_mask, evicted, evicted_stride,
+                                     evicted_count, stats, status, req_num, key_space, query_count, free_target);
+}
+
+}  // namespace
+
+extern "C" int asu_lru_step(void* stream, int32_t* token_to_slot, int32_t* slot_to_token, int32_t* lru_order,
+                            int32_t* free_stack, int32_t* free_count, const int32_t* query, int32_t* slot_out,
+                            uint8_t* hit_mask, uint8_t* install_mask, int32_t* evicted, uint32_t evicted_stride,
+                            int32_t* evicted_count, int64_t* stats, int32_t* status, uint32_t req_num,
+                            uint32_t key_space, uint32_t slot_count, uint32_t query_count, uint32_t free_target) {
+    return lru_step<false>(stream, token_to_slot, slot_to_token, lru_order, free_stack, free_count, query, nullptr,
+                           slot_out, hit_mask, install_mask, evicted, evicted_stride, evicted_count, stats, status,
+                           req_num, key_space, slot_count, query_count, free_target);
+}
+
+extern "C" int asu_lru_step_host_query(void* stream, int32_t* token_to_slot, int32_t* slot_to_token,
+                                       int32_t* lru_order, int32_t* free_stack, int32_t* free_count,
+                                       const int32_t* query, int32_t* query_copy, int32_t* slot_out,
+                                       uint8_t* hit_mask, uint8_t* install_mask, int32_t* evicted,
+                                       uint32_t evicted_stride, int32_t* evicted_count, int64_t* stats,
+                                       int32_t* status, uint32_t req_num, uint32_t key_space, uint32_t slot_count,
+                                       uint32_t query_count, uint32_t free_target) {
+    return lru_step<true>(stream, token_to_slot, slot_to_token, lru_order, free_stack, free_count, query, query_copy,
+                          slot_out, hit_mask, install_mask, evicted, evicted_stride, evicted_count, stats, status,
+                          req_num, key_space, slot_count, query_count, free_target);
 }

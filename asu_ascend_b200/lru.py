@@ -12,6 +12,7 @@ layers.
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -84,6 +85,32 @@ class LruSlotPools:
                 o.hit.data_ptr(), o.install.data_ptr(), o.evicted.data_ptr(), o.evicted.shape[1],
                 o.evicted_count.data_ptr(), self.stats.data_ptr(), self.status.data_ptr(), self.req_num,
                 self.key_space, self.slot_count, self.query_count, self.free_target), "asu_lru_step")
+        return o
+
+    def step_from_host(self, query: torch.Tensor, query_copy: torch.Tensor, out: LruStepOutput | None = None,
+                       stream: torch.cuda.Stream | None = None) -> LruStepOutput:
+        """``step`` for a top-k in pinned host memory: ``query`` [R, Q] int32 is read by the step
+        itself over the host link (no upload), and copied to ``query_copy`` [R, Q] int32 in HBM for
+        the swap-in that follows.  Asynchronous: keep ``query`` unchanged until the step is done."""
+        if query.dtype != torch.int32 or query.device.type != "cpu" or not query.is_contiguous():
+            raise RuntimeError("query must be a contiguous int32 tensor in pinned host memory")
+        if query_copy.dtype != torch.int32 or query_copy.device != self.device or not query_copy.is_contiguous():
+            raise RuntimeError("query_copy must be a contiguous int32 tensor on the pool's device")
+        shape = (self.req_num, self.query_count)
+        if tuple(query.shape) != shape or tuple(query_copy.shape) != shape:
+            raise RuntimeError(f"query and query_copy must be [{self.req_num}, {self.query_count}]")
+        qdev = ctypes.c_void_p()
+        check(lib.asu_host_device_pointer(query.data_ptr(), ctypes.byref(qdev)),
+              "query: device address of pinned memory")
+        o = out or self._out
+        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        with torch.cuda.device(self.device):
+            check(lib.asu_lru_step_host_query(
+                s, self.token_to_slot.data_ptr(), self.slot_to_token.data_ptr(), self.lru_order.data_ptr(),
+                self.free_stack.data_ptr(), self.free_count.data_ptr(), qdev.value, query_copy.data_ptr(),
+                o.slot.data_ptr(), o.hit.data_ptr(), o.install.data_ptr(), o.evicted.data_ptr(), o.evicted.shape[1],
+                o.evicted_count.data_ptr(), self.stats.data_ptr(), self.status.data_ptr(), self.req_num,
+                self.key_space, self.slot_count, self.query_count, self.free_target), "asu_lru_step_host_query")
         return o
 
     def check_status(self, ignore: int = ST_SHORTAGE) -> None:

@@ -654,17 +654,15 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     q_ins = [torch.empty((R, cfg.topk), dtype=torch.int32, device=dev) for _ in range(2 if overlap else 1)]
     ev2 = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K_steps)]
     ev2_warm = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(W)]
-    # per step and layer: the top-k upload's own interval; per step: the host time to queue the step
-    up_ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(L)] for _ in range(K_steps)]
-    up_warm = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(L)] for _ in range(W)]
-    host_ms: list[float] = []
-    # The top-k goes up and the slot ids and hit mask come back through the host mapping, copied by
-    # the SMs (asu_mapped_copy): with several GPUs on one host the copy engines get the smallest share
-    # of it.  The read-back runs on a second stream while the swap-in reads host rows: the two run in
-    # opposite directions of the host link.
+    host_ms: list[float] = []  # per step: the host time to queue the step
+    # The LRU step reads the top-k from pinned host memory itself and leaves an HBM copy for the
+    # swap-in (asu_lru_step_host_query), and the slot ids and hit mask come back through the host
+    # mapping, copied by the SMs (asu_mapped_copy): no copy engine is involved (with several GPUs on
+    # one host the copy engines get the smallest share of it).  The read-back runs on a second stream
+    # while the swap-in reads host rows: the two run in opposite directions of the host link.
     copy_stream = torch.cuda.Stream(dev)
 
-    def e2e_steps(first, events, uploads, host=None):
+    def e2e_steps(first, events, host=None):
         for k, (e0, e1) in enumerate(events):
             flush()
             torch.cuda._sleep(spin)
@@ -674,10 +672,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
                 o = outs[(k * L + layer) % 2]
                 q_in = q_ins[layer % len(q_ins)]
                 pipe.before_step(layer)
-                uploads[k][layer][0].record()
-                mapped_copy_(q_in, q_host[first + k, layer])  # SM reads of the pinned top-k
-                uploads[k][layer][1].record()
-                pools[layer].step(q_in, out=o)
+                pools[layer].step_from_host(q_host[first + k, layer], q_in, out=o)
                 copy_stream.wait_stream(main)
                 with torch.cuda.stream(copy_stream):
                     mapped_copy_(slot_host, o.slot)  # SM writes into pinned host memory
@@ -695,11 +690,10 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             if host is not None:
                 host.append((time.perf_counter() - t0) * 1e3)
 
-    e2e_steps(base2, ev2_warm, up_warm)  # untimed warm-up of the e2e loop's own code (first uses happen here)
+    e2e_steps(base2, ev2_warm)  # untimed warm-up of the e2e loop's own code (first uses happen here)
     rank_sync(torch)
-    e2e_steps(base2 + W, ev2, up_ev, host_ms)
+    e2e_steps(base2 + W, ev2, host_ms)
     rank_sync(torch)
-    upload_ms = [sum(a.elapsed_time(b) for a, b in step) for step in up_ev]
     e2e_ms = [e[0].elapsed_time(e[1]) for e in ev2]
     floor_us = event_floor_us(torch, flush, spin, K_steps)
     for p in pools:
@@ -715,7 +709,7 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
     # per rank: its GPU's H2D copy alone and with every rank copying, its timed step and swap-in
     # intervals and the rows installed into its own requests (every rank takes part)
     by_rank = rows_by_rank([h2d_alone, h2d_peak, sum(step_ms), sum(swapin_ms), installs, local_rank, sum(e2e_ms),
-                            sum(upload_ms), statistics.median(host_ms)], dev)
+                            statistics.median(host_ms)], dev)
     job_stats = reduce_stats(torch.stack([p.stats for p in pools])).cpu().tolist()  # end-of-run (NCCL)
     job_req = cfg.req if cfg.strong else cfg.req * world
     idx_per_step = job_req * cfg.topk * L
@@ -784,8 +778,8 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             "e2e": {"value": idx_per_step * K_steps / (max_e2e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": R * cfg.topk * 4 * L, "d2h_bytes_per_step": R * cfg.topk * 5 * L},
             "gpu_launches": 2 * launches,
-            # the e2e region adds the top-k upload and the two read-backs (asu_mapped_copy) per layer
-            "gpu_launches_e2e": 5 * launches,
+            # the e2e region adds the two read-backs (asu_mapped_copy) per layer
+            "gpu_launches_e2e": 4 * launches,
             "job_stats": dict(zip(LruSlotPools.STAT_NAMES, job_stats)),
             "host_cpus_bound": len(bound_cpus),
             "note_step_time": ("the step's event bracket (layers pipelined over two streams)" if overlap else
@@ -794,9 +788,9 @@ def run_resolver(args, cfg: ResolverCfg, world: int, rank: int, local_rank: int)
             "step_bracket_ms_p50": statistics.median(bracket_ms),
             "balance": balance_info,
             "by_rank": [{"gpu": int(d), "h2d_alone_gbs": a, "h2d_concurrent_gbs": c, "step_ms_sum": st,
-                         "swapin_ms_sum": sw, "e2e_ms_sum": e, "e2e_upload_ms_sum": up, "e2e_host_ms_p50": hm,
+                         "swapin_ms_sum": sw, "e2e_ms_sum": e, "e2e_host_ms_p50": hm,
                          "own_installs": int(n), "own_rows_gbs": n * cfg.row / (sw * 1e-3) / 1e9 if sw > 0 else None}
-                        for a, c, st, sw, n, d, e, up, hm in by_rank],
+                        for a, c, st, sw, n, d, e, hm in by_rank],
             "placement": PLACEMENT,
             "step_ms_by_rank0": step_ms,
             "e2e_ms_by_rank0": e2e_ms,

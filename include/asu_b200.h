@@ -174,6 +174,19 @@ int asu_lru_step(void* stream, int32_t* token_to_slot, int32_t* slot_to_token, i
                  int32_t* evicted_count, int64_t* stats, int32_t* status, uint32_t req_num, uint32_t key_space,
                  uint32_t slot_count, uint32_t query_count, uint32_t free_target);
 
+/* asu_lru_step for a caller whose top-k is in pinned host memory (no reference counterpart: the
+ * reference's top-k comes from the indexer on the NPU).  `query` is the device address of the
+ * pinned, mapped [req_num, query_count] buffer (asu_host_device_pointer): the step reads it over
+ * the host link itself instead of after an upload, and stores every query to query_copy
+ * [req_num, query_count] in HBM, the copy a following asu_swapin_gather reads.  Everything else
+ * as asu_lru_step. */
+int asu_lru_step_host_query(void* stream, int32_t* token_to_slot, int32_t* slot_to_token, int32_t* lru_order,
+                            int32_t* free_stack, int32_t* free_count, const int32_t* query, int32_t* query_copy,
+                            int32_t* slot_out, uint8_t* hit_mask, uint8_t* install_mask, int32_t* evicted,
+                            uint32_t evicted_stride, int32_t* evicted_count, int64_t* stats, int32_t* status,
+                            uint32_t req_num, uint32_t key_space, uint32_t slot_count, uint32_t query_count,
+                            uint32_t free_target);
+
 /* ======================================================================
  * swap-in gather: host row pool -> HBM slot pool
  * ==================================================================== */
