@@ -64,16 +64,16 @@ METRIC = "resolved KV indices/sec (lookup + LRU maintain + swap-in gather)"
 # Ascend 910B (docs/archive/hbm_kvcache_lookup_recommendations.md:32) = 2.93e8 indices/s.
 REF_LOOKUP_IDX_PER_S = 50 * 2048 / 350e-6
 # From the ncu captures summarised in profiles/ (first timed step of the resolver workload):
-SWAPIN_PCIE_READ_BYTES_PER_LAUNCH = 54.31e9 * 652.4e-6   # pcie__read_bytes.sum.per_second x duration
-SWAPIN_NCU_INSTALLS = 0.182 * 128 * 2048                  # rows swapped in by that launch (~18.2% miss)
-LRU_DRAM_BYTES_PER_LAUNCH = 21.19e6 + 0.062e6             # dram__bytes_read.sum + dram__bytes_write.sum
+SWAPIN_PCIE_READ_BYTES_PER_LAUNCH = 35.43e6              # pcie__read_bytes.sum of one launch
+SWAPIN_NCU_INSTALLS = 0.1815 * 128 * 2048                 # rows swapped in by that launch (~18.15% miss)
+LRU_DRAM_BYTES_PER_LAUNCH = 21.17e6 + 0.03e6              # dram__bytes_read.sum + dram__bytes_write.sum
 GATHER_DRAM_BYTES_PER_LAUNCH = 13.82e6                     # lookup workload, gather_vec4_kernel
 RESOLVE_DRAM_BYTES_PER_CALL = 0.903e6                      # decode workload, resolve_kernel (rows copied in-cluster)
 WRITEBACK_PCIE_WRITE_BYTES_PER_LAUNCH = 59.06e9 * 1.918e-3  # pcie__write_bytes.sum.per_second x duration
 OPS_LOOKUP_DRAM_BYTES_PER_LAUNCH = 0.213e6                  # ops workload, req 8 mixed
 # where the traffic figures come from (the kernel source they were captured on)
-SWAPIN_TRAFFIC_SOURCE = "profiles/swapin_bulk_kernel_c2.md (ncu capture of the swap-in kernel as of commit bd3ed66)"
-LRU_TRAFFIC_SOURCE = "profiles/lru_step_kernel_c2.md (ncu capture of the LRU kernel as of commit 9193eab)"
+SWAPIN_TRAFFIC_SOURCE = "profiles/swapin_bulk_kernel_c2.md (ncu capture of the swap-in kernel as of commit 5ddb8f8)"
+LRU_TRAFFIC_SOURCE = "profiles/lru_step_kernel_c2.md (ncu capture of the LRU kernel as of commit 5ddb8f8)"
 
 
 @dataclass
