@@ -603,6 +603,8 @@ int dispatch_s(cudaStream_t s, const LruResolveArgs& a) {
     if (a.S <= 2u * kThreads) return launch<IPT_Q, 2>(s, a);
     if (a.S <= 4u * kThreads) return launch<IPT_Q, 4>(s, a);
     if (a.S <= 8u * kThreads) return launch<IPT_Q, 8>(s, a);
+    // 8192 + 2048 managed slots: 12 order entries on each of 854 threads instead of 16 on 640
+    if (a.S <= 12u * kThreads) return launch<IPT_Q, 12>(s, a);
     return launch<IPT_Q, 16>(s, a);
 }
 
