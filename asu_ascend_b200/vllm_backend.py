@@ -27,6 +27,8 @@ from __future__ import annotations
 
 import functools
 
+import torch
+
 from . import sparse_mla
 
 SINGLE_REQ_ID = "__single_req__"  # patch line 486
@@ -86,6 +88,11 @@ def asu_flashmla_sparse_impl():
             name = getattr(self, "_asu_layer_name", None)
             if not use_asu_kv_cache(manager, name, attn_metadata):
                 return None
+            if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+                raise RuntimeError(
+                    "the ASU decode path cannot be captured in a CUDA graph: it decides on the host, "
+                    "every step, whether to reset or extend the request and passes its length to the "
+                    "resolver; run attention eagerly (vLLM cudagraph mode PIECEWISE or NONE)")
             ctx = prepare_asu_layer_context(manager, name, attn_metadata)
             kv = kv_c_and_k_pe_cache.reshape(*kv_c_and_k_pe_cache.shape[:2], -1)
             slots = sparse_mla.resolve_topk(ctx, topk_indices.contiguous(), attn_metadata.block_table[0], kv)
@@ -125,19 +132,43 @@ def asu_flashmla_sparse_impl():
 
 
 @functools.lru_cache(maxsize=1)
+def asu_flashmla_sparse_builder():
+    """vLLM's FlashMLA-sparse metadata builder, declared without CUDA-graph support.
+
+    The ASU decode path decides on the host, every step, whether the request is new (reset) or one
+    token longer (mark) and passes the request's length to the resolver as a scalar, as the
+    reference does (patch/0003, patch lines 480-499).  A full CUDA graph of attention would replay
+    the first step's decisions and length forever, so vLLM must keep attention out of its graphs
+    (it then captures the rest of the model piecewise)."""
+    from vllm.v1.attention.backend import AttentionCGSupport
+    from vllm.v1.attention.backends.mla.flashmla_sparse import FlashMLASparseMetadataBuilder
+
+    class ASUFlashMLASparseMetadataBuilder(FlashMLASparseMetadataBuilder):
+        _cudagraph_support = AttentionCGSupport.NEVER
+
+    return ASUFlashMLASparseMetadataBuilder
+
+
+@functools.lru_cache(maxsize=1)
 def asu_flashmla_sparse_backend():
-    """vLLM's FlashMLASparseBackend with ASUFlashMLASparseImpl as its implementation class; the
-    name, metadata builder, cache shape and kernel-block sizes stay vLLM's."""
+    """vLLM's FlashMLASparseBackend with ASUFlashMLASparseImpl as its implementation class and a
+    metadata builder without CUDA-graph support (``asu_flashmla_sparse_builder``); the name,
+    metadata, cache shape and kernel-block sizes stay vLLM's."""
     from vllm.v1.attention.backends.mla.flashmla_sparse import FlashMLASparseBackend
 
     impl = asu_flashmla_sparse_impl()
+    builder = asu_flashmla_sparse_builder()
 
     class ASUFlashMLASparseBackend(FlashMLASparseBackend):
         @staticmethod
         def get_impl_cls():
             return impl
 
-    for cls in (ASUFlashMLASparseBackend, impl):  # importable by name (vLLM resolves class paths)
+        @staticmethod
+        def get_builder_cls():
+            return builder
+
+    for cls in (ASUFlashMLASparseBackend, impl, builder):  # importable by name (vLLM resolves class paths)
         cls.__module__ = __name__
         cls.__qualname__ = cls.__name__
     return ASUFlashMLASparseBackend
@@ -149,6 +180,8 @@ def __getattr__(name):
         return asu_flashmla_sparse_backend()
     if name == "ASUFlashMLASparseImpl":
         return asu_flashmla_sparse_impl()
+    if name == "ASUFlashMLASparseMetadataBuilder":
+        return asu_flashmla_sparse_builder()
     raise AttributeError(name)
 
 

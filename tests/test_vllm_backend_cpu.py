@@ -156,3 +156,27 @@ def test_registered_override_resolves_to_the_asu_backend():
         _ATTN_OVERRIDES.clear()
         _ATTN_OVERRIDES.update(before)
         V.asu_flashmla_sparse_impl().asu_manager = None
+
+
+def test_asu_backend_keeps_attention_out_of_full_cuda_graphs(monkeypatch):
+    """The ASU path decides on the host every step (reset or mark, the request's length): its
+    builder declares no CUDA-graph support, and a capture that reaches the path anyway is refused."""
+    pytest.importorskip("vllm")
+    from vllm.v1.attention.backend import AttentionCGSupport
+    from vllm.v1.attention.backends.mla.flashmla_sparse import FlashMLASparseMetadataBuilder
+
+    backend = V.asu_flashmla_sparse_backend()
+    builder = backend.get_builder_cls()
+    assert builder is V.ASUFlashMLASparseMetadataBuilder and issubclass(builder, FlashMLASparseMetadataBuilder)
+    assert builder.get_cudagraph_support(None, None) == AttentionCGSupport.NEVER
+    assert FlashMLASparseMetadataBuilder.get_cudagraph_support(None, None) != AttentionCGSupport.NEVER
+
+    cls = V.asu_flashmla_sparse_impl()
+    impl = cls.__new__(cls)
+    impl._asu_layer_name = "l0"
+    m = FakeManager()
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: True)
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: True)
+    with pytest.raises(RuntimeError, match="CUDA graph"):
+        impl._asu_resolve(None, None, _md(asu_kv_cache_manager=m))
+    assert m.calls == []  # refused before any reset or mark was queued
