@@ -135,8 +135,8 @@ def parse_args():
                         "of rank i for i < N/2 (skips the unbalanced calibration round; checks the balanced path on "
                         "any box)")
     p.add_argument("--shared-pool", action="store_true",
-                   help="1 GPU: back the host pool with a shared-memory file registered with the GPU "
-                        "(the pool every rank uses on N > 1 GPUs) instead of cudaHostAlloc")
+                   help="back the host pool with a shared-memory file registered with the GPU (the pool "
+                        "--balance needs) instead of cudaHostAlloc")
     p.add_argument("--no-spread", action="store_true",
                    help="N > 1 with more GPUs visible than ranks: rank r on GPU r instead of the measured placement "
                         "(the GPUs that share the host link least)")
