@@ -11,7 +11,9 @@ one decode-layer resolve for 128 requests per GPU --
 Each request has a 128K-token context, a top-k of 2048 per step with reuse + Zipf locality
 (70% of the previous step's ids kept, 30% Zipf(1.1) draws), 8192 HBM slots and an LRU free
 target of 2048.  Requests are sharded over GPUs: N GPUs run N x 128 independent requests
-(weak scaling) with no collective on the data path.  The pools are first filled by
+(weak scaling) with no collective on the data path; with fewer ranks than visible GPUs the
+ranks take the GPUs that share the host link least (measured at start-up, `--no-spread` turns it
+off).  The pools are first filled by
 `--prefill` untimed steps so the timed steps run at the steady-state miss rate.
 
 Other workloads (`--workload`):
